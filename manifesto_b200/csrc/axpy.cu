@@ -1,0 +1,208 @@
+// axpy.cu -- K5 (mf_axpy) and K6 (mf_scalar_broadcast).
+//
+// mf_axpy replaces axpyDevice.Axpy (runtime/axpy.go:13-15, called at
+// :84-90) and the host loops of axpyOntoHost (:115-117 and :145-147 with
+// the BF16/F16 re-encode of float32VectorBytes, :171-194):
+//   y[i] = encode( decode(y[i]) + alpha * decode(x[i]) )
+// with the float32 multiply and add rounded separately (the amd64 Go
+// build does not contract), or one fused rounding when fused_fma is set.
+// mf_scalar_broadcast replaces applyScalarBroadcast
+// (runtime/executor_math.go:195-234) plus its store encode.
+// Both stream 16-element chunks with 128-bit accesses.
+// Roofline: HBM; axpy moves 3 * sizeof(dtype) bytes per element.
+#include "mf_runtime.h"
+#include "mf_vec.cuh"
+
+namespace mf {
+namespace {
+
+constexpr int kThreads = 256;
+
+template <int FUSED>
+__device__ __forceinline__ float axpy_op(float y, float x, float alpha) {
+    if constexpr (FUSED) return __fmaf_rn(alpha, x, y);
+    else return __fadd_rn(y, __fmul_rn(alpha, x));
+}
+
+template <int DT, int FUSED>
+__global__ void __launch_bounds__(kThreads) axpy_vec_kernel(void* __restrict__ y, const void* __restrict__ x,
+                                                           int64_t n, float alpha) {
+    constexpr int B = dtype_bytes(DT);
+    const int64_t nchunks = n / kChunk;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nchunks; c += stride) {
+        RawChunk<B> ry, rx;
+        load_raw<B>(y, c, ry);
+        load_raw<B>(x, c, rx);
+        float vy[kChunk], vx[kChunk];
+        decode16<DT>(ry, vy);
+        decode16<DT>(rx, vx);
+#pragma unroll
+        for (int k = 0; k < kChunk; ++k) vy[k] = axpy_op<FUSED>(vy[k], vx[k], alpha);
+        encode16<DT>(vy, ry, 0);
+        store_raw<B>(y, c, ry);
+    }
+    if (blockIdx.x == 0) {
+        const int64_t i = nchunks * kChunk + threadIdx.x;
+        if (i < n) {
+            const float r = axpy_op<FUSED>(load_as_f32<DT>(y, i), load_as_f32<DT>(x, i), alpha);
+            store_code<DT>(y, i, encode_f32<DT>(r, 0));
+        }
+    }
+}
+
+template <int DT, int FUSED>
+__global__ void __launch_bounds__(kThreads) axpy_scalar_kernel(void* __restrict__ y, const void* __restrict__ x,
+                                                              int64_t n, float alpha) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const float r = axpy_op<FUSED>(load_as_f32<DT>(y, i), load_as_f32<DT>(x, i), alpha);
+        store_code<DT>(y, i, encode_f32<DT>(r, 0));
+    }
+}
+
+template <int DT>
+int launch_axpy(void* y, const void* x, int64_t n, float alpha, int fused, cudaStream_t s) {
+    if (aligned16(y) && aligned16(x)) {
+        const int64_t blocks = stream_grid(n / kChunk + 1, kThreads, 8);
+        if (fused) axpy_vec_kernel<DT, 1><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(y, x, n, alpha);
+        else axpy_vec_kernel<DT, 0><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(y, x, n, alpha);
+    } else {
+        const int64_t blocks = stream_grid(n, kThreads, 8);
+        if (fused) axpy_scalar_kernel<DT, 1><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(y, x, n, alpha);
+        else axpy_scalar_kernel<DT, 0><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(y, x, n, alpha);
+    }
+    MF_LAUNCH_CHECK("mf_axpy launch");
+    return MF_OK;
+}
+
+// ------------------------------------------------------ scalar broadcast
+
+template <int OP>
+__device__ __forceinline__ float scalar_op(float v, float s) {
+    if constexpr (OP == MF_SCALAR_ADD) return __fadd_rn(v, s);
+    else if constexpr (OP == MF_SCALAR_SUB) return __fsub_rn(v, s);
+    else if constexpr (OP == MF_SCALAR_MUL) return __fmul_rn(v, s);
+    else return __fdiv_rn(v, s);
+}
+
+template <int SRC, int DST, int OP>
+__global__ void __launch_bounds__(kThreads) scalar_vec_kernel(const void* __restrict__ src, void* __restrict__ dst,
+                                                             int64_t n, float scalar) {
+    const int64_t nchunks = n / kChunk;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nchunks; c += stride) {
+        RawChunk<dtype_bytes(SRC)> r;
+        load_raw<dtype_bytes(SRC)>(src, c, r);
+        float v[kChunk];
+        decode16<SRC>(r, v);
+#pragma unroll
+        for (int k = 0; k < kChunk; ++k) v[k] = scalar_op<OP>(v[k], scalar);
+        RawChunk<dtype_bytes(DST)> o;
+        encode16<DST>(v, o, 0);
+        store_raw<dtype_bytes(DST)>(dst, c, o);
+    }
+    if (blockIdx.x == 0) {
+        const int64_t i = nchunks * kChunk + threadIdx.x;
+        if (i < n) store_code<DST>(dst, i, encode_f32<DST>(scalar_op<OP>(load_as_f32<SRC>(src, i), scalar), 0));
+    }
+}
+
+template <int SRC, int DST, int OP>
+__global__ void __launch_bounds__(kThreads) scalar_elem_kernel(const void* __restrict__ src, void* __restrict__ dst,
+                                                              int64_t n, float scalar) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+        store_code<DST>(dst, i, encode_f32<DST>(scalar_op<OP>(load_as_f32<SRC>(src, i), scalar), 0));
+}
+
+template <int SRC, int DST, int OP>
+void launch_scalar_op(const void* src, void* dst, int64_t n, float scalar, cudaStream_t s) {
+    constexpr bool kVecSrc = SRC == MF_DT_F32 || SRC == MF_DT_F16 || SRC == MF_DT_BF16 || SRC == MF_DT_F8E4M3 ||
+                             SRC == MF_DT_F8E5M2;
+    if (kVecSrc && aligned16(src) && aligned16(dst)) {
+        if constexpr (kVecSrc) {
+            const int64_t blocks = stream_grid(n / kChunk + 1, kThreads, 8);
+            scalar_vec_kernel<SRC, DST, OP><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, scalar);
+        }
+    } else {
+        const int64_t blocks = stream_grid(n, kThreads, 8);
+        scalar_elem_kernel<SRC, DST, OP><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, scalar);
+    }
+}
+
+template <int SRC, int DST>
+void dispatch_op(int op, const void* src, void* dst, int64_t n, float scalar, cudaStream_t s) {
+    switch (op) {
+    case MF_SCALAR_ADD: launch_scalar_op<SRC, DST, MF_SCALAR_ADD>(src, dst, n, scalar, s); break;
+    case MF_SCALAR_SUB: launch_scalar_op<SRC, DST, MF_SCALAR_SUB>(src, dst, n, scalar, s); break;
+    case MF_SCALAR_MUL: launch_scalar_op<SRC, DST, MF_SCALAR_MUL>(src, dst, n, scalar, s); break;
+    default: launch_scalar_op<SRC, DST, MF_SCALAR_DIV>(src, dst, n, scalar, s); break;
+    }
+}
+
+template <int SRC>
+void dispatch_scalar_dst(int dst_dt, int op, const void* src, void* dst, int64_t n, float scalar, cudaStream_t s) {
+    switch (dst_dt) {
+    case MF_DT_F32: dispatch_op<SRC, MF_DT_F32>(op, src, dst, n, scalar, s); break;
+    case MF_DT_F16: dispatch_op<SRC, MF_DT_F16>(op, src, dst, n, scalar, s); break;
+    default: dispatch_op<SRC, MF_DT_BF16>(op, src, dst, n, scalar, s); break;
+    }
+}
+
+}  // namespace
+}  // namespace mf
+
+using namespace mf;
+
+extern "C" int mf_axpy(void* y, const void* x, int64_t n, float alpha, int dtype, int fused_fma,
+                       mf_stream stream) {
+    MF_ENTER();
+    if (n < 0) return fail(MF_ERR_SHAPE_INVALID, "mf_axpy: negative element count %lld", (long long)n);
+    if (!is_float_store_dtype(dtype))
+        return fail(MF_ERR_DTYPE_UNSUPPORTED, "mf_axpy: dtype %d unsupported (F32, F16, BF16)", dtype);
+    if (n == 0) return MF_OK;
+    if (!y || !x) return fail(MF_ERR_INVALID_ARGUMENT, "mf_axpy: NULL buffer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (dtype) {
+    case MF_DT_F32: return launch_axpy<MF_DT_F32>(y, x, n, alpha, fused_fma, s);
+    case MF_DT_BF16: return launch_axpy<MF_DT_BF16>(y, x, n, alpha, fused_fma, s);
+    default: return launch_axpy<MF_DT_F16>(y, x, n, alpha, fused_fma, s);
+    }
+}
+
+extern "C" int mf_scalar_broadcast(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, float scalar,
+                                   int op, mf_stream stream) {
+    MF_ENTER();
+    if (n < 0) return fail(MF_ERR_SHAPE_INVALID, "mf_scalar_broadcast: negative element count %lld", (long long)n);
+    if (op < MF_SCALAR_ADD || op > MF_SCALAR_DIV)
+        return fail(MF_ERR_INVALID_ARGUMENT, "math.scalar_broadcast: unsupported op %d", op);
+    if (op == MF_SCALAR_DIV && scalar == 0.0f)
+        return fail(MF_ERR_INVALID_ARGUMENT, "math.scalar_broadcast: scalar divisor must be nonzero");
+    if (!is_decodable(src_dtype))
+        return fail(MF_ERR_DTYPE_UNSUPPORTED, "mf_scalar_broadcast: source dtype %d unsupported", src_dtype);
+    if (!is_float_store_dtype(dst_dtype))
+        return fail(MF_ERR_DTYPE_UNSUPPORTED, "mf_scalar_broadcast: destination dtype %d unsupported", dst_dtype);
+    if (n == 0) return MF_OK;
+    if (!src || !dst) return fail(MF_ERR_INVALID_ARGUMENT, "mf_scalar_broadcast: NULL buffer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (src_dtype) {
+    case MF_DT_F32: dispatch_scalar_dst<MF_DT_F32>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_F16: dispatch_scalar_dst<MF_DT_F16>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_BF16: dispatch_scalar_dst<MF_DT_BF16>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_F8E4M3: dispatch_scalar_dst<MF_DT_F8E4M3>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_F8E5M2: dispatch_scalar_dst<MF_DT_F8E5M2>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_F64: dispatch_scalar_dst<MF_DT_F64>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_I64: dispatch_scalar_dst<MF_DT_I64>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_I32: dispatch_scalar_dst<MF_DT_I32>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_I16: dispatch_scalar_dst<MF_DT_I16>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_I8: dispatch_scalar_dst<MF_DT_I8>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_I4: dispatch_scalar_dst<MF_DT_I4>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_U64: dispatch_scalar_dst<MF_DT_U64>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_U32: dispatch_scalar_dst<MF_DT_U32>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_U16: dispatch_scalar_dst<MF_DT_U16>(dst_dtype, op, src, dst, n, scalar, s); break;
+    default: dispatch_scalar_dst<MF_DT_U8>(dst_dtype, op, src, dst, n, scalar, s); break;
+    }
+    MF_LAUNCH_CHECK("mf_scalar_broadcast launch");
+    return MF_OK;
+}

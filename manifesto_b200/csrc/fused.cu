@@ -1,0 +1,487 @@
+// fused.cu -- K7: fused elementwise chains (mf_fused_compile / mf_fused_launch)
+// and the fused chain -> amax -> FP8 pipeline (mf_fused_fp8).
+//
+// A compiled kernel is manifesto's optimizer.FusionAST (optimizer/fusion_ast.go:86-113)
+// in postfix form.  Its evaluation follows codegen.evalCPU (codegen/cpu.go:126-212):
+// inputs decode to float32; Add/Sub/Mul/Div/Max/Min/Neg/Abs/ReLU/LeakyReLU run in
+// float32; Sqrt/Exp/Log/Sigmoid/Tanh/Silu/Gelu run in float64 and round to float32;
+// the result is encoded to the output dtype with the reference store encoders.
+//
+// Two device bodies:
+//   * a generic interpreter: the program travels by value in the kernel parameter
+//     block (constant bank, warp-uniform reads), one element per thread-iteration,
+//     a small evaluation stack in thread-local memory;
+//   * a hand-specialised body for Mul(Silu(Add(Mul(x, g), b)), y) with BF16
+//     inputs/output and g, b broadcast along the last dimension -- the SwiGLU-style
+//     chain manifesto's fuser builds (optimizer/optimizer_test.go SwiGLU case).  It
+//     streams 16-element chunks with 128-bit accesses and evaluates SiLU in float32
+//     (ex2.approx + fast reciprocal); the result is within 1 BF16 ulp of the
+//     float64 reference formula, which is the tolerance this chain is held to.
+//     With amax requested it folds max|out| on the BF16 bit patterns (__vmaxu2).
+#include <algorithm>
+#include <cstring>
+#include <new>
+
+#include "mf_internal.h"
+#include "mf_runtime.h"
+#include "mf_vec.cuh"
+
+// optimizer.NodeType values, optimizer/fusion_ast.go:32-65
+enum NodeType : int32_t {
+    NODE_INVALID = 0, NODE_INPUT, NODE_CONSTANT, NODE_ADD, NODE_SUB, NODE_MUL, NODE_DIV, NODE_MAX, NODE_MIN,
+    NODE_NEG, NODE_ABS, NODE_SQRT, NODE_EXP, NODE_LOG, NODE_RELU, NODE_SIGMOID, NODE_TANH, NODE_SILU,
+    NODE_GELU, NODE_LEAKY_RELU
+};
+
+struct mf_fused_kernel_s;
+
+namespace mf {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxStack = 16;
+
+struct FusedProgram {
+    int32_t n_nodes;
+    int32_t n_inputs;
+    int32_t out_dtype;
+    int32_t pad;
+    int8_t op[MF_FUSED_MAX_NODES];
+    int8_t arg[MF_FUSED_MAX_NODES];
+    uint32_t const_bits[MF_FUSED_MAX_CONSTS];  // float32(node.Value) bit patterns
+    int32_t in_dtype[MF_FUSED_MAX_INPUTS];
+    int64_t in_bcast[MF_FUSED_MAX_INPUTS];
+};
+
+struct InputPtrs {
+    const void* p[MF_FUSED_MAX_INPUTS];
+};
+
+int arity(int op) {
+    switch (op) {
+    case NODE_INPUT: case NODE_CONSTANT: return 0;
+    case NODE_NEG: case NODE_ABS: case NODE_SQRT: case NODE_EXP: case NODE_LOG: case NODE_RELU:
+    case NODE_SIGMOID: case NODE_TANH: case NODE_SILU: case NODE_GELU: case NODE_LEAKY_RELU: return 1;
+    case NODE_ADD: case NODE_SUB: case NODE_MUL: case NODE_DIV: case NODE_MAX: case NODE_MIN: return 2;
+    default: return -1;
+    }
+}
+
+// ------------------------------------------------------ interpreter
+
+__device__ __forceinline__ float load_input(int dt, const void* p, int64_t i) {
+    switch (dt) {
+    case MF_DT_BF16: return load_as_f32<MF_DT_BF16>(p, i);
+    case MF_DT_F16: return load_as_f32<MF_DT_F16>(p, i);
+    default: return load_as_f32<MF_DT_F32>(p, i);
+    }
+}
+
+// sqrt(2/pi) in float64: Go folds the constant 2/math.Pi exactly and math.Sqrt
+// rounds once (codegen/cpu.go:198).
+__device__ __forceinline__ double gelu_k() { return sqrt(0.63661977236758134307553505349005744813783858296182579499); }
+
+__device__ __forceinline__ float apply_unary(int op, float v) {
+    switch (op) {
+    case NODE_NEG: return -v;
+    case NODE_ABS: return v < 0.0f ? -v : v;
+    case NODE_SQRT: return f64_to_f32(sqrt(static_cast<double>(v)));
+    case NODE_EXP: return f64_to_f32(exp(static_cast<double>(v)));
+    case NODE_LOG: return f64_to_f32(log(static_cast<double>(v)));
+    case NODE_RELU: return v < 0.0f ? 0.0f : v;
+    case NODE_SIGMOID: return f64_to_f32(__drcp_rn(__dadd_rn(1.0, exp(-static_cast<double>(v)))));
+    case NODE_TANH: return f64_to_f32(tanh(static_cast<double>(v)));
+    case NODE_SILU: {
+        const double d = static_cast<double>(v);
+        return f64_to_f32(__ddiv_rn(d, __dadd_rn(1.0, exp(-d))));
+    }
+    case NODE_GELU: {
+        const double d = static_cast<double>(v);
+        const double cube = __dmul_rn(__dmul_rn(__dmul_rn(0.044715, d), d), d);
+        const double inner = __dmul_rn(gelu_k(), __dadd_rn(d, cube));
+        return f64_to_f32(__dmul_rn(__dmul_rn(0.5, d), __dadd_rn(1.0, tanh(inner))));
+    }
+    case NODE_LEAKY_RELU: return v >= 0.0f ? v : __fmul_rn(0.01f, v);
+    default: return 0.0f;
+    }
+}
+
+__device__ __forceinline__ float apply_binary(int op, float a, float b) {
+    switch (op) {
+    case NODE_ADD: return __fadd_rn(a, b);
+    case NODE_SUB: return __fsub_rn(a, b);
+    case NODE_MUL: return __fmul_rn(a, b);
+    case NODE_DIV: return __fdiv_rn(a, b);
+    case NODE_MAX: return a > b ? a : b;
+    case NODE_MIN: return a < b ? a : b;
+    default: return 0.0f;
+    }
+}
+
+__device__ __forceinline__ int64_t bcast_index(int64_t i, int64_t l) {
+    if (l <= 0) return i;
+    if (i < (int64_t(1) << 32) && l < (int64_t(1) << 32))
+        return static_cast<int64_t>(static_cast<uint32_t>(i) % static_cast<uint32_t>(l));
+    return i % l;
+}
+
+__device__ __forceinline__ float eval_program(const FusedProgram& p, const InputPtrs& in, int64_t i) {
+    float st[kMaxStack];
+    int sp = 0;
+    for (int k = 0; k < p.n_nodes; ++k) {
+        const int op = p.op[k];
+        if (op == NODE_INPUT) {
+            const int j = p.arg[k];
+            st[sp++] = load_input(p.in_dtype[j], in.p[j], bcast_index(i, p.in_bcast[j]));
+        } else if (op == NODE_CONSTANT) {
+            st[sp++] = __uint_as_float(p.const_bits[p.arg[k]]);
+        } else if (op >= NODE_ADD && op <= NODE_MIN) {
+            const float b = st[--sp];
+            st[sp - 1] = apply_binary(op, st[sp - 1], b);
+        } else {
+            st[sp - 1] = apply_unary(op, st[sp - 1]);
+        }
+    }
+    return st[0];
+}
+
+template <int ODT>
+__global__ void __launch_bounds__(kThreads) fused_interp_kernel(const __grid_constant__ FusedProgram p,
+                                                               const __grid_constant__ InputPtrs in,
+                                                               void* __restrict__ out, int64_t n,
+                                                               float* __restrict__ d_amax) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    float m = 0.0f;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint32_t code = encode_f32<ODT>(eval_program(p, in, i), 0);
+        store_code<ODT>(out, i, code);
+        if (d_amax) {
+            // |stored value|, NaN ignored
+            float a;
+            if constexpr (ODT == MF_DT_F32) a = fabsf(__uint_as_float(code));
+            else if constexpr (ODT == MF_DT_BF16) a = fabsf(__uint_as_float(code << 16));
+            else a = fabsf(__uint_as_float(f16_to_f32bits(code)));
+            m = (a > m) ? a : m;
+        }
+    }
+    if (d_amax) {
+        // block reduce
+        __shared__ float part[kThreads / 32];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            m = threadIdx.x < kThreads / 32 ? part[threadIdx.x] : 0.0f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (threadIdx.x == 0 && m > 0.0f) atomicMax(reinterpret_cast<unsigned int*>(d_amax), __float_as_uint(m));
+        }
+    }
+}
+
+// -------------------------------------------- SwiGLU-style specialisation
+
+// Mul(Silu(Add(Mul(x, g), b)), y): x, y full-size BF16; g, b BF16 of length L
+// (L % 16 == 0) read at i mod L; BF16 output.
+template <bool AMAX>
+__global__ void __launch_bounds__(kThreads) swiglu_bf16_kernel(const uint4* __restrict__ x, const uint4* __restrict__ y,
+                                                              const uint4* __restrict__ g, const uint4* __restrict__ b,
+                                                              uint4* __restrict__ out, int64_t nchunks,
+                                                              uint32_t row_chunks, float* __restrict__ d_amax) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    uint32_t key = 0;
+    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nchunks; c += stride) {
+        const uint32_t rc = static_cast<uint32_t>(c % row_chunks);
+        const uint4 x0 = ld_stream(x + 2 * c), x1 = ld_stream(x + 2 * c + 1);
+        const uint4 y0 = ld_stream(y + 2 * c), y1 = ld_stream(y + 2 * c + 1);
+        const uint4 g0 = __ldg(g + 2 * rc), g1 = __ldg(g + 2 * rc + 1);
+        const uint4 b0 = __ldg(b + 2 * rc), b1 = __ldg(b + 2 * rc + 1);
+        const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        const uint32_t yw[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+        const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        uint32_t ow[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            float r[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float xv = __uint_as_float(h ? (xw[k] & 0xffff0000u) : (xw[k] << 16));
+                const float yv = __uint_as_float(h ? (yw[k] & 0xffff0000u) : (yw[k] << 16));
+                const float gv = __uint_as_float(h ? (gw[k] & 0xffff0000u) : (gw[k] << 16));
+                const float bv = __uint_as_float(h ? (bw[k] & 0xffff0000u) : (bw[k] << 16));
+                const float t = __fadd_rn(__fmul_rn(xv, gv), bv);
+                // silu(t) = t / (1 + e^-t); e^-t = 2^(-t*log2(e))
+                const float e = exp2f_approx(__fmul_rn(t, -1.4426950408889634f));
+                const float s = __fmul_rn(t, rcp_approx(__fadd_rn(1.0f, e)));
+                r[h] = __fmul_rn(s, yv);
+            }
+            ow[k] = f32x2_to_bf16x2(r[0], r[1]);
+            if constexpr (AMAX) {
+                const uint32_t a = ow[k] & 0x7fff7fffu;
+                key = __vmaxu2(key, a & ~__vcmpgtu2(a, 0x7f807f80u));
+            }
+        }
+        st_stream(out + 2 * c, make_uint4(ow[0], ow[1], ow[2], ow[3]));
+        st_stream(out + 2 * c + 1, make_uint4(ow[4], ow[5], ow[6], ow[7]));
+    }
+    if constexpr (AMAX) {
+        float m = __uint_as_float(max(key & 0xffffu, key >> 16) << 16);
+        __shared__ float part[kThreads / 32];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            m = threadIdx.x < kThreads / 32 ? part[threadIdx.x] : 0.0f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (threadIdx.x == 0 && m > 0.0f) atomicMax(reinterpret_cast<unsigned int*>(d_amax), __float_as_uint(m));
+        }
+    }
+}
+
+}  // namespace
+}  // namespace mf
+
+struct mf_fused_kernel_s {
+    mf::FusedProgram prog;
+    int max_depth = 0;
+    // specialisation: 0 = interpreter, 1 = SwiGLU-style BF16 chain
+    int special = 0;
+    int sx = -1, sg = -1, sb = -1, sy = -1;  // input slots of x, g, b, y
+    int64_t bcast_len = 0;
+};
+
+namespace mf {
+namespace {
+
+// Host-side float32(float64) with the amd64 Go rule (NaN keeps top payload bits).
+uint32_t host_f64_to_f32_bits(double d) {
+    uint64_t b;
+    std::memcpy(&b, &d, 8);
+    if (d != d) return static_cast<uint32_t>((b >> 32) & 0x80000000u) | 0x7fc00000u | static_cast<uint32_t>((b >> 29) & 0x7fffffu);
+    const float f = static_cast<float>(d);
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    return u;
+}
+
+// Postfix subtree ending at `end` (inclusive): returns its first index.
+int subtree_start(const mf_fused_kernel_s& k, int end) {
+    int need = 1, i = end;
+    while (need > 0 && i >= 0) {
+        need += arity(k.prog.op[i]) - 1;
+        if (need == 0) return i;
+        --i;
+    }
+    return i;
+}
+
+// Node index -> input slot if it is an Input leaf, else -1.
+int leaf_input(const mf_fused_kernel_s& k, int idx) {
+    return k.prog.op[idx] == NODE_INPUT ? k.prog.arg[idx] : -1;
+}
+
+// Try to recognise Mul(Silu(Add(Mul(x, g), b)), y) in any operand order.
+void detect_swiglu(mf_fused_kernel_s& k) {
+    const FusedProgram& p = k.prog;
+    const int n = p.n_nodes;
+    if (n != 8 || p.out_dtype != MF_DT_BF16 || p.op[n - 1] != NODE_MUL) return;
+    // children of the root: [a][b] where b ends at n-2
+    const int rb_end = n - 2, rb_start = subtree_start(k, rb_end);
+    const int ra_end = rb_start - 1;
+    int silu_end, y_idx;
+    if (p.op[rb_end] == NODE_SILU && ra_end >= 0 && subtree_start(k, ra_end) == 0 && leaf_input(k, ra_end) >= 0 && ra_end == 0) {
+        silu_end = rb_end; y_idx = 0;
+    } else if (p.op[ra_end] == NODE_SILU && rb_start == rb_end && leaf_input(k, rb_end) >= 0) {
+        silu_end = ra_end; y_idx = rb_end;
+    } else {
+        return;
+    }
+    const int add_end = silu_end - 1;
+    if (p.op[add_end] != NODE_ADD) return;
+    const int add_b_end = add_end - 1, add_b_start = subtree_start(k, add_b_end);
+    const int add_a_end = add_b_start - 1;
+    int mul_end, b_idx;
+    if (p.op[add_b_end] == NODE_MUL && add_a_end >= 0 && leaf_input(k, add_a_end) >= 0) {
+        mul_end = add_b_end; b_idx = add_a_end;
+    } else if (p.op[add_a_end] == NODE_MUL && add_b_start == add_b_end && leaf_input(k, add_b_end) >= 0) {
+        mul_end = add_a_end; b_idx = add_b_end;
+    } else {
+        return;
+    }
+    if (mul_end < 2 || leaf_input(k, mul_end - 1) < 0 || leaf_input(k, mul_end - 2) < 0) return;
+    int s1 = leaf_input(k, mul_end - 2), s2 = leaf_input(k, mul_end - 1);
+    const int sb = leaf_input(k, b_idx), sy = leaf_input(k, y_idx);
+    // x and y full-size; g and b broadcast with the same period
+    if (p.in_bcast[s1] > 0 && p.in_bcast[s2] == 0) std::swap(s1, s2);
+    const int sx = s1, sg = s2;
+    const int64_t l = p.in_bcast[sg];
+    if (p.in_bcast[sx] != 0 || p.in_bcast[sy] != 0 || l <= 0 || l % 16 != 0 || p.in_bcast[sb] != l) return;
+    for (int s : {sx, sg, sb, sy})
+        if (p.in_dtype[s] != MF_DT_BF16) return;
+    k.special = 1;
+    k.sx = sx; k.sg = sg; k.sb = sb; k.sy = sy;
+    k.bcast_len = l;
+}
+
+template <int ODT>
+void launch_interp(const mf_fused_kernel_s& k, const InputPtrs& in, void* out, int64_t n, float* d_amax,
+                   cudaStream_t s) {
+    const int64_t blocks = stream_grid(n, kThreads, 8);
+    fused_interp_kernel<ODT><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(k.prog, in, out, n, d_amax);
+}
+
+int launch_fused(const mf_fused_kernel_s& k, const void* const* inputs, void* out, int64_t n, float* d_amax,
+                 cudaStream_t s) {
+    InputPtrs in{};
+    for (int j = 0; j < k.prog.n_inputs; ++j) {
+        if (!inputs[j]) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fused_launch: input %d is NULL", j);
+        in.p[j] = inputs[j];
+    }
+    bool special = k.special == 1 && n % 16 == 0 && aligned16(out);
+    if (special)
+        for (int j : {k.sx, k.sg, k.sb, k.sy}) special = special && aligned16(inputs[j]);
+    if (special) {
+        const int64_t nchunks = n / 16;
+        const int64_t blocks = stream_grid(nchunks, kThreads, 8);
+        const uint32_t row_chunks = static_cast<uint32_t>(k.bcast_len / 16);
+        if (d_amax)
+            swiglu_bf16_kernel<true><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
+                static_cast<const uint4*>(inputs[k.sx]), static_cast<const uint4*>(inputs[k.sy]),
+                static_cast<const uint4*>(inputs[k.sg]), static_cast<const uint4*>(inputs[k.sb]),
+                static_cast<uint4*>(out), nchunks, row_chunks, d_amax);
+        else
+            swiglu_bf16_kernel<false><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
+                static_cast<const uint4*>(inputs[k.sx]), static_cast<const uint4*>(inputs[k.sy]),
+                static_cast<const uint4*>(inputs[k.sg]), static_cast<const uint4*>(inputs[k.sb]),
+                static_cast<uint4*>(out), nchunks, row_chunks, nullptr);
+    } else {
+        switch (k.prog.out_dtype) {
+        case MF_DT_BF16: launch_interp<MF_DT_BF16>(k, in, out, n, d_amax, s); break;
+        case MF_DT_F16: launch_interp<MF_DT_F16>(k, in, out, n, d_amax, s); break;
+        default: launch_interp<MF_DT_F32>(k, in, out, n, d_amax, s); break;
+        }
+    }
+    MF_LAUNCH_CHECK("mf_fused_launch");
+    return MF_OK;
+}
+
+}  // namespace
+}  // namespace mf
+
+using namespace mf;
+
+extern "C" int mf_fused_compile(const mf_fused_program* program, mf_fused_kernel* kernel) {
+    if (!program || !kernel) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fused_compile: NULL argument");
+    *kernel = nullptr;
+    const mf_fused_program& p = *program;
+    if (p.n_nodes <= 0 || p.n_nodes > MF_FUSED_MAX_NODES || !p.op || !p.arg)
+        return fail(MF_ERR_INVALID_ARGUMENT, "codegen cuda: program has %d nodes (1..%d)", p.n_nodes, MF_FUSED_MAX_NODES);
+    if (p.n_inputs < 0 || p.n_inputs > MF_FUSED_MAX_INPUTS || (p.n_inputs > 0 && !p.in_dtype))
+        return fail(MF_ERR_INVALID_ARGUMENT, "codegen cuda: %d inputs (0..%d)", p.n_inputs, MF_FUSED_MAX_INPUTS);
+    if (p.n_consts < 0 || p.n_consts > MF_FUSED_MAX_CONSTS || (p.n_consts > 0 && !p.consts))
+        return fail(MF_ERR_INVALID_ARGUMENT, "codegen cuda: %d constants (0..%d)", p.n_consts, MF_FUSED_MAX_CONSTS);
+    if (!is_float_store_dtype(p.out_dtype))
+        return fail(MF_ERR_DTYPE_UNSUPPORTED, "codegen cuda: output dtype %d unsupported", p.out_dtype);
+    mf_fused_kernel_s* k = new (std::nothrow) mf_fused_kernel_s();
+    if (!k) return fail(MF_ERR_ALLOCATOR_EXHAUSTED, "mf_fused_compile: out of host memory");
+    std::memset(&k->prog, 0, sizeof k->prog);
+    k->prog.n_nodes = p.n_nodes;
+    k->prog.n_inputs = p.n_inputs;
+    k->prog.out_dtype = p.out_dtype;
+    for (int j = 0; j < p.n_inputs; ++j) {
+        if (!is_float_store_dtype(p.in_dtype[j])) {
+            delete k;
+            return fail(MF_ERR_DTYPE_UNSUPPORTED, "codegen cuda: input %d dtype %d unsupported", j, p.in_dtype[j]);
+        }
+        const int64_t l = p.in_bcast ? p.in_bcast[j] : 0;
+        if (l < 0) {
+            delete k;
+            return fail(MF_ERR_SHAPE_INVALID, "codegen cuda: input %d broadcast length %lld", j, (long long)l);
+        }
+        k->prog.in_dtype[j] = p.in_dtype[j];
+        k->prog.in_bcast[j] = l;
+    }
+    for (int c = 0; c < p.n_consts; ++c) k->prog.const_bits[c] = host_f64_to_f32_bits(p.consts[c]);
+    int depth = 0, max_depth = 0;
+    for (int i = 0; i < p.n_nodes; ++i) {
+        const int op = p.op[i];
+        const int a = arity(op);
+        if (a < 0) {
+            delete k;
+            return fail(MF_ERR_INVALID_ARGUMENT, "codegen cuda: node %d has invalid type %d", i, op);
+        }
+        if (op == NODE_INPUT && (p.arg[i] < 0 || p.arg[i] >= p.n_inputs)) {
+            delete k;
+            return fail(MF_ERR_INVALID_ARGUMENT, "codegen cuda: node %d reads input %d of %d", i, p.arg[i], p.n_inputs);
+        }
+        if (op == NODE_CONSTANT && (p.arg[i] < 0 || p.arg[i] >= p.n_consts)) {
+            delete k;
+            return fail(MF_ERR_INVALID_ARGUMENT, "codegen cuda: node %d reads constant %d of %d", i, p.arg[i], p.n_consts);
+        }
+        if (depth < a) {
+            delete k;
+            return fail(MF_ERR_INVALID_ARGUMENT, "codegen cuda: node %d (%d) lacks operands", i, op);
+        }
+        depth += 1 - a;
+        max_depth = std::max(max_depth, depth);
+        k->prog.op[i] = static_cast<int8_t>(op);
+        k->prog.arg[i] = static_cast<int8_t>((op == NODE_INPUT || op == NODE_CONSTANT) ? p.arg[i] : 0);
+    }
+    if (depth != 1) {
+        delete k;
+        return fail(MF_ERR_INVALID_ARGUMENT, "codegen cuda: program leaves %d values, expected 1", depth);
+    }
+    if (max_depth > kMaxStack) {
+        delete k;
+        return fail(MF_ERR_INVALID_ARGUMENT, "codegen cuda: expression needs %d stack slots (max %d)", max_depth, kMaxStack);
+    }
+    k->max_depth = max_depth;
+    detect_swiglu(*k);
+    *kernel = k;
+    return MF_OK;
+}
+
+extern "C" int mf_fused_destroy(mf_fused_kernel kernel) {
+    delete kernel;
+    return MF_OK;
+}
+
+extern "C" int mf_fused_is_specialised(mf_fused_kernel kernel, int* specialised) {
+    if (!kernel || !specialised) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fused_is_specialised: NULL argument");
+    *specialised = kernel->special;
+    return MF_OK;
+}
+
+extern "C" int mf_fused_launch(mf_fused_kernel kernel, const void* const* inputs, void* out, int64_t n, float* d_amax,
+                               mf_stream stream) {
+    MF_ENTER();
+    if (!kernel) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fused_launch: kernel is NULL");
+    if (n < 0) return fail(MF_ERR_SHAPE_INVALID, "mf_fused_launch: negative element count %lld", (long long)n);
+    if (n == 0) return MF_OK;
+    if (!out || (kernel->prog.n_inputs > 0 && !inputs))
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_fused_launch: NULL buffer");
+    return launch_fused(*kernel, inputs, out, n, d_amax, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mf_fused_fp8(mf_fused_kernel kernel, const void* const* inputs, void* precast, void* dst, int fp8_dtype,
+                            float* d_amax, float* d_scale_inv, int64_t n, int compat, mf_stream stream) {
+    MF_ENTER();
+    if (!kernel) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fused_fp8: kernel is NULL");
+    if (n < 0) return fail(MF_ERR_SHAPE_INVALID, "mf_fused_fp8: negative element count %lld", (long long)n);
+    if (!is_fp8(fp8_dtype)) return fail(MF_ERR_DTYPE_UNSUPPORTED, "mf_fused_fp8: dtype %d is not FP8", fp8_dtype);
+    if (compat != MF_COMPAT_REFERENCE && compat != MF_COMPAT_OCP)
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_fused_fp8: unknown compat mode %d", compat);
+    if (!d_amax) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fused_fp8: d_amax is NULL");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    MF_CUDA_CHECK(cudaMemsetAsync(d_amax, 0, sizeof(float), s));
+    if (n == 0) return MF_OK;
+    if (!precast || !dst || (kernel->prog.n_inputs > 0 && !inputs))
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_fused_fp8: NULL buffer");
+    int rc = launch_fused(*kernel, inputs, precast, n, d_amax, s);
+    if (rc) return rc;
+    return launch_scaled_cast(precast, kernel->prog.out_dtype, dst, fp8_dtype, d_amax, d_scale_inv, n, compat, s);
+}

@@ -1,0 +1,160 @@
+// int4.cu -- K4: packed Int4 group dequantisation (mf_int4_dequant_grouped).
+//
+//   out[r, c] = encode( float32(q[r, c]) * float32(scale[r, c / group]) )
+//
+// q: row-major [rows, cols] signed nibbles, element 2i in the low nibble of
+// byte i (dtype/int4.go:12-40, dtype/convert/decoders.go:262-289).
+// scales: row-major [rows, ceil(cols / group)].  The product of a nibble
+// in [-8, 7] and a BF16/F16 scale is exact in float32, so the only rounding
+// is the final store encode (NewBfloat16FromFloat32, dtype/bfloat16.go:41-55).
+//
+// Fast path (cols % 32 == 0, group % 32 == 0, 16-byte aligned buffers): a
+// thread owns 32 consecutive elements of one row and one group: one 128-bit
+// load of 16 packed bytes, one scale load (shared by the 4 threads of a
+// 128-element group, served from L1), and four 128-bit stores of BF16.
+// Nibble -> float uses the exponent trick: (n ^ 8) | 0x4B000000 is the
+// float 2^23 + q + 8, so q = that - (2^23 + 8) exactly, with no I2F.
+// Roofline: HBM, 0.5 B in + 2 B out per element + scales.
+#include "mf_runtime.h"
+#include "mf_vec.cuh"
+
+namespace mf {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kElems = 32;  // elements per thread-chunk (16 packed bytes)
+
+template <int SDT>
+__device__ __forceinline__ float load_scale(const void* s, int64_t i) {
+    if constexpr (SDT == MF_DT_BF16) return __uint_as_float(static_cast<uint32_t>(__ldg(static_cast<const uint16_t*>(s) + i)) << 16);
+    else if constexpr (SDT == MF_DT_F16) return __uint_as_float(f16_to_f32bits(__ldg(static_cast<const uint16_t*>(s) + i)));
+    else return __ldg(static_cast<const float*>(s) + i);
+}
+
+// nibble k (0..7) of w as float32 (exact), via 2^23 + (q + 8) - (2^23 + 8)
+__device__ __forceinline__ float nibble_f32(uint32_t w, int k) {
+    const uint32_t bits = ((w >> (4 * k)) & 0xfu) ^ 0x4B000008u;
+    return __fsub_rn(__uint_as_float(bits), 8388616.0f);
+}
+
+template <int SDT, int ODT>
+__global__ void __launch_bounds__(kThreads) int4_dequant_vec_kernel(const uint4* __restrict__ q,
+                                                                   const void* __restrict__ scales,
+                                                                   void* __restrict__ out, int64_t nchunks,
+                                                                   uint32_t chunks_per_row,
+                                                                   uint32_t chunks_per_group,
+                                                                   int64_t ngroups) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nchunks; c += stride) {
+        const uint4 packed = ld_stream(q + c);
+        const int64_t row = c / chunks_per_row;
+        const uint32_t cr = static_cast<uint32_t>(c - row * chunks_per_row);
+        const float s = load_scale<SDT>(scales, row * ngroups + cr / chunks_per_group);
+        const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
+        float v[kElems];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[8 * j + k] = __fmul_rn(nibble_f32(w[j], k), s);
+        }
+        if constexpr (ODT == MF_DT_F32) {
+            uint4* o = reinterpret_cast<uint4*>(out) + c * 8;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                st_stream(o + j, make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                                            __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3])));
+        } else {
+            uint4* o = reinterpret_cast<uint4*>(out) + c * 4;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t p[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float lo = v[8 * j + 2 * k], hi = v[8 * j + 2 * k + 1];
+                    p[k] = (ODT == MF_DT_BF16) ? f32x2_to_bf16x2(lo, hi) : f32x2_to_f16x2(lo, hi);
+                }
+                st_stream(o + j, make_uint4(p[0], p[1], p[2], p[3]));
+            }
+        }
+    }
+}
+
+// Any shape with even cols: one element per thread-iteration.
+template <int SDT, int ODT>
+__global__ void __launch_bounds__(kThreads) int4_dequant_scalar_kernel(const uint8_t* __restrict__ q,
+                                                                      const void* __restrict__ scales,
+                                                                      void* __restrict__ out, int64_t rows,
+                                                                      int64_t cols, int64_t group,
+                                                                      int64_t ngroups) {
+    const int64_t n = rows * cols;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < n; e += stride) {
+        const int64_t r = e / cols;
+        const int64_t col = e - r * cols;
+        const float qv = load_as_f32<MF_DT_I4>(q, e);
+        const float v = __fmul_rn(qv, load_scale<SDT>(scales, r * ngroups + col / group));
+        store_code<ODT>(out, e, encode_f32<ODT>(v, 0));
+    }
+}
+
+template <int SDT, int ODT>
+int launch(const void* q, const void* scales, void* out, int64_t rows, int64_t cols, int64_t group,
+           cudaStream_t s) {
+    const int64_t ngroups = (cols + group - 1) / group;
+    const bool vec = (cols % kElems == 0) && (group % kElems == 0) && aligned16(q) && aligned16(out) &&
+                     (cols / kElems) < (int64_t(1) << 31);
+    if (vec) {
+        const int64_t nchunks = rows * cols / kElems;
+        const int64_t blocks = stream_grid(nchunks, kThreads, 8);
+        int4_dequant_vec_kernel<SDT, ODT><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
+            static_cast<const uint4*>(q), scales, out, nchunks, static_cast<uint32_t>(cols / kElems),
+            static_cast<uint32_t>(group / kElems), ngroups);
+    } else {
+        const int64_t blocks = stream_grid(rows * cols, kThreads, 8);
+        int4_dequant_scalar_kernel<SDT, ODT><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
+            static_cast<const uint8_t*>(q), scales, out, rows, cols, group, ngroups);
+    }
+    MF_LAUNCH_CHECK("mf_int4_dequant_grouped launch");
+    return MF_OK;
+}
+
+template <int SDT>
+int dispatch_out(int out_dtype, const void* q, const void* scales, void* out, int64_t rows, int64_t cols,
+                 int64_t group, cudaStream_t s) {
+    switch (out_dtype) {
+    case MF_DT_BF16: return launch<SDT, MF_DT_BF16>(q, scales, out, rows, cols, group, s);
+    case MF_DT_F16: return launch<SDT, MF_DT_F16>(q, scales, out, rows, cols, group, s);
+    default: return launch<SDT, MF_DT_F32>(q, scales, out, rows, cols, group, s);
+    }
+}
+
+}  // namespace
+}  // namespace mf
+
+using namespace mf;
+
+extern "C" int mf_int4_dequant_grouped(const void* q, const void* scales, int scale_dtype, void* out,
+                                       int out_dtype, int64_t rows, int64_t cols, int64_t group,
+                                       mf_stream stream) {
+    MF_ENTER();
+    if (rows < 0 || cols < 0)
+        return fail(MF_ERR_SHAPE_INVALID, "mf_int4_dequant_grouped: negative shape [%lld, %lld]",
+                    (long long)rows, (long long)cols);
+    if (cols % 2 != 0)
+        return fail(MF_ERR_SHAPE_INVALID, "mf_int4_dequant_grouped: cols (%lld) must be even", (long long)cols);
+    if (group <= 0)
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_int4_dequant_grouped: group must be positive, got %lld",
+                    (long long)group);
+    if (scale_dtype != MF_DT_BF16 && scale_dtype != MF_DT_F16 && scale_dtype != MF_DT_F32)
+        return fail(MF_ERR_DTYPE_UNSUPPORTED, "mf_int4_dequant_grouped: scale dtype %d unsupported", scale_dtype);
+    if (!is_float_store_dtype(out_dtype))
+        return fail(MF_ERR_DTYPE_UNSUPPORTED, "mf_int4_dequant_grouped: output dtype %d unsupported", out_dtype);
+    if (rows == 0 || cols == 0) return MF_OK;
+    if (!q || !scales || !out) return fail(MF_ERR_INVALID_ARGUMENT, "mf_int4_dequant_grouped: NULL buffer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (scale_dtype) {
+    case MF_DT_BF16: return dispatch_out<MF_DT_BF16>(out_dtype, q, scales, out, rows, cols, group, s);
+    case MF_DT_F16: return dispatch_out<MF_DT_F16>(out_dtype, q, scales, out, rows, cols, group, s);
+    default: return dispatch_out<MF_DT_F32>(out_dtype, q, scales, out, rows, cols, group, s);
+    }
+}

@@ -1,0 +1,616 @@
+// quant.cu -- K8 per-tensor amax-scaled FP8 cast and K9 grouped
+// whole-checkpoint quantisation.
+//
+// The reference has no amax, scale or quantize operation (its only cast
+// is shape.cast); the semantics here are composed from its primitives:
+//   amax      = max |v| (NaN ignored, as Go's '>' never selects NaN)
+//   scale     = fp8_max / amax in float32, 1 if amax is 0 or not finite
+//   q         = NewF8E4M3FromFloat32(v * scale)   (dtype/fp8.go:77-136)
+//               or NewF8E5M2FromFloat32           (dtype/fp8.go:190-249)
+//   scale_inv = amax / fp8_max in float32, 1 if amax is 0 or not finite
+//
+// amax is computed on the integer bit patterns: for every IEEE-like format
+// |v| orders like (bits & ~sign) once NaN codes are excluded, so a BF16
+// pair is folded with one masked __vmaxu2 and the maximum code is decoded
+// once at the end.  Roofline: HBM; amax reads src once, the cast reads src
+// and writes 1 B per element.
+//
+// Checkpoint quantisation: each rank owns one contiguous chunk of every
+// tensor.  One descriptor table (passed by value as the kernel parameter,
+// so nothing is allocated) lists the chunks; the chunks are cut into
+// 16384-element tiles and each CTA walks a contiguous range of tiles, so a
+// CTA crosses few tensor boundaries and reduces its per-tensor maximum
+// once per crossing.  Pass 1 (amax) and pass 2 (cast) are one launch each
+// per 512 chunks; between them an NCCL max all-reduce of the amax vector
+// makes the scales global.
+#include <algorithm>
+#include <mutex>
+
+#include "mf_internal.h"
+#include "mf_runtime.h"
+#include "mf_vec.cuh"
+
+namespace mf {
+namespace {
+
+constexpr int kThreads = 256;
+
+__host__ __device__ inline float fp8_max(int fp8_dtype) { return fp8_dtype == MF_DT_F8E5M2 ? 57344.0f : 448.0f; }
+
+__device__ __forceinline__ float scale_from_amax(float amax, int fp8_dtype) {
+    const bool ok = (amax > 0.0f) && (amax < __int_as_float(0x7f800000));
+    return ok ? __fdiv_rn(fp8_max(fp8_dtype), amax) : 1.0f;
+}
+__device__ __forceinline__ float scale_inv_from_amax(float amax, int fp8_dtype) {
+    const bool ok = (amax > 0.0f) && (amax < __int_as_float(0x7f800000));
+    return ok ? __fdiv_rn(amax, fp8_max(fp8_dtype)) : 1.0f;
+}
+
+// ---------------------------------------------------------------- amax
+
+// Magnitude key of one element: monotone in |v|, 0 for NaN.
+template <int DT>
+struct MagKey;
+template <>
+struct MagKey<MF_DT_F32> {
+    // running max of (bits & 0x7fffffff) over non-NaN values
+    static __device__ __forceinline__ uint32_t fold(const RawChunk<4>& r, uint32_t m) {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const uint32_t a = r.w[k] & 0x7fffffffu;
+            m = (a <= 0x7f800000u && a > m) ? a : m;
+        }
+        return m;
+    }
+    static __device__ __forceinline__ float to_f32(uint32_t m) { return __uint_as_float(m); }
+};
+template <int DT>
+struct MagKey16 {
+    // two halves per word: (h & 0x7fff) with NaN codes (> nan_floor) zeroed
+    static __device__ __forceinline__ uint32_t fold(const RawChunk<2>& r, uint32_t m, uint32_t nan_floor2) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t a = r.w[k] & 0x7fff7fffu;
+            const uint32_t nan_mask = __vcmpgtu2(a, nan_floor2);
+            m = __vmaxu2(m, a & ~nan_mask);
+        }
+        return m;
+    }
+};
+template <>
+struct MagKey<MF_DT_BF16> {
+    static __device__ __forceinline__ uint32_t fold(const RawChunk<2>& r, uint32_t m) {
+        return MagKey16<MF_DT_BF16>::fold(r, m, 0x7f807f80u);
+    }
+    static __device__ __forceinline__ float to_f32(uint32_t m) {
+        const uint32_t h = max(m & 0xffffu, m >> 16);
+        return __uint_as_float(h << 16);
+    }
+};
+template <>
+struct MagKey<MF_DT_F16> {
+    static __device__ __forceinline__ uint32_t fold(const RawChunk<2>& r, uint32_t m) {
+        return MagKey16<MF_DT_F16>::fold(r, m, 0x7c007c00u);
+    }
+    static __device__ __forceinline__ float to_f32(uint32_t m) {
+        const uint32_t h = max(m & 0xffffu, m >> 16);
+        return __uint_as_float(f16_to_f32bits(h));
+    }
+};
+template <int DT>
+struct MagKey8 {
+    static __device__ __forceinline__ uint32_t fold(const RawChunk<1>& r, uint32_t m, uint32_t nan_floor4) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t a = r.w[k] & 0x7f7f7f7fu;
+            const uint32_t nan_mask = __vcmpgtu4(a, nan_floor4);
+            m = __vmaxu4(m, a & ~nan_mask);
+        }
+        return m;
+    }
+    static __device__ __forceinline__ uint32_t top(uint32_t m) {
+        return max(max(m & 0xffu, (m >> 8) & 0xffu), max((m >> 16) & 0xffu, m >> 24));
+    }
+};
+template <>
+struct MagKey<MF_DT_F8E4M3> {
+    static __device__ __forceinline__ uint32_t fold(const RawChunk<1>& r, uint32_t m) {
+        return MagKey8<MF_DT_F8E4M3>::fold(r, m, 0x7e7e7e7eu);
+    }
+    static __device__ __forceinline__ float to_f32(uint32_t m) {
+        return __uint_as_float(e4m3_to_f32bits(MagKey8<MF_DT_F8E4M3>::top(m)));
+    }
+};
+template <>
+struct MagKey<MF_DT_F8E5M2> {
+    static __device__ __forceinline__ uint32_t fold(const RawChunk<1>& r, uint32_t m) {
+        return MagKey8<MF_DT_F8E5M2>::fold(r, m, 0x7c7c7c7cu);
+    }
+    static __device__ __forceinline__ float to_f32(uint32_t m) {
+        return __uint_as_float(e5m2_to_f32bits(MagKey8<MF_DT_F8E5M2>::top(m)));
+    }
+};
+
+__device__ __forceinline__ float warp_max(float m) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    return m;
+}
+
+// Block-wide maximum of a non-negative float; result valid in thread 0.
+__device__ __forceinline__ float block_max(float m) {
+    __shared__ float partial[kThreads / 32];
+    m = warp_max(m);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();  // partial[] may still be read by a previous call
+    if (lane == 0) partial[warp] = m;
+    __syncthreads();
+    if (warp == 0) {
+        m = lane < kThreads / 32 ? partial[lane] : 0.0f;
+        m = warp_max(m);
+    }
+    return m;
+}
+
+__device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
+    if (v > 0.0f) atomicMax(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
+}
+
+// |v| of one element, NaN -> 0 (for scalar tails)
+template <int DT>
+__device__ __forceinline__ float abs_or_zero(const void* p, int64_t i) {
+    const float a = fabsf(load_as_f32<DT>(p, i));
+    return (a == a) ? a : 0.0f;
+}
+
+template <int SRC>
+__global__ void __launch_bounds__(kThreads) amax_vec_kernel(const void* __restrict__ src, int64_t n,
+                                                           float* __restrict__ amax) {
+    const int64_t nchunks = n / kChunk;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    uint32_t key = 0;
+    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nchunks; c += stride) {
+        RawChunk<dtype_bytes(SRC)> r;
+        load_raw<dtype_bytes(SRC)>(src, c, r);
+        key = MagKey<SRC>::fold(r, key);
+    }
+    float m = MagKey<SRC>::to_f32(key);
+    if (blockIdx.x == 0) {
+        const int64_t i = nchunks * kChunk + threadIdx.x;
+        if (i < n) m = fmaxf(m, abs_or_zero<SRC>(src, i));
+    }
+    m = block_max(m);
+    if (threadIdx.x == 0) atomic_max_nonneg(amax, m);
+}
+
+template <int SRC>
+__global__ void __launch_bounds__(kThreads) amax_scalar_kernel(const void* __restrict__ src, int64_t n,
+                                                              float* __restrict__ amax) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    float m = 0.0f;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+        m = fmaxf(m, abs_or_zero<SRC>(src, i));
+    m = block_max(m);
+    if (threadIdx.x == 0) atomic_max_nonneg(amax, m);
+}
+
+// --------------------------------------------------------- scaled cast
+
+template <int FP8>
+__device__ __forceinline__ uint32_t encode_fp8(float v, int compat) {
+    return encode_f32<FP8>(v, compat);
+}
+
+template <int SRC, int FP8, int COMPAT>
+__device__ __forceinline__ void cast_chunk(const void* src, void* dst, int64_t c, float scale) {
+    RawChunk<dtype_bytes(SRC)> r;
+    load_raw<dtype_bytes(SRC)>(src, c, r);
+    float v[kChunk];
+    decode16<SRC>(r, v);
+#pragma unroll
+    for (int k = 0; k < kChunk; ++k) v[k] = __fmul_rn(v[k], scale);
+    RawChunk<1> o;
+    encode16<FP8>(v, o, COMPAT);
+    store_raw<1>(dst, c, o);
+}
+
+template <int SRC, int FP8, int COMPAT>
+__global__ void __launch_bounds__(kThreads) scaled_cast_vec_kernel(const void* __restrict__ src,
+                                                                  void* __restrict__ dst, int64_t n,
+                                                                  const float* __restrict__ d_amax,
+                                                                  float* __restrict__ d_scale_inv) {
+    const float amax = *d_amax;
+    const float scale = scale_from_amax(amax, FP8);
+    if (d_scale_inv && blockIdx.x == 0 && threadIdx.x == 0) *d_scale_inv = scale_inv_from_amax(amax, FP8);
+    const int64_t nchunks = n / kChunk;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nchunks; c += stride)
+        cast_chunk<SRC, FP8, COMPAT>(src, dst, c, scale);
+    if (blockIdx.x == 0) {
+        const int64_t i = nchunks * kChunk + threadIdx.x;
+        if (i < n) store_code<FP8>(dst, i, encode_fp8<FP8>(__fmul_rn(load_as_f32<SRC>(src, i), scale), COMPAT));
+    }
+}
+
+template <int SRC, int FP8>
+__global__ void __launch_bounds__(kThreads) scaled_cast_scalar_kernel(const void* __restrict__ src,
+                                                                     void* __restrict__ dst, int64_t n,
+                                                                     const float* __restrict__ d_amax,
+                                                                     float* __restrict__ d_scale_inv, int compat) {
+    const float amax = *d_amax;
+    const float scale = scale_from_amax(amax, FP8);
+    if (d_scale_inv && blockIdx.x == 0 && threadIdx.x == 0) *d_scale_inv = scale_inv_from_amax(amax, FP8);
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+        store_code<FP8>(dst, i, encode_fp8<FP8>(__fmul_rn(load_as_f32<SRC>(src, i), scale), compat));
+}
+
+bool is_vec_src(int dt) { return dt == MF_DT_F32 || dt == MF_DT_F16 || dt == MF_DT_BF16 || dt == MF_DT_F8E4M3 || dt == MF_DT_F8E5M2; }
+
+template <int SRC>
+void amax_dispatch(const void* src, int64_t n, float* d_amax, cudaStream_t s) {
+    if (aligned16(src)) {
+        const int64_t blocks = stream_grid(n / kChunk + 1, kThreads, 8);
+        amax_vec_kernel<SRC><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, n, d_amax);
+    } else {
+        const int64_t blocks = stream_grid(n, kThreads, 8);
+        amax_scalar_kernel<SRC><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, n, d_amax);
+    }
+}
+
+template <int SRC, int FP8>
+void cast_dispatch(const void* src, void* dst, int64_t n, const float* d_amax, float* d_scale_inv, int compat,
+                   cudaStream_t s) {
+    if (aligned16(src) && aligned16(dst)) {
+        const int64_t blocks = stream_grid(n / kChunk + 1, kThreads, 8);
+        if (compat)
+            scaled_cast_vec_kernel<SRC, FP8, 1><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, d_amax, d_scale_inv);
+        else
+            scaled_cast_vec_kernel<SRC, FP8, 0><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, d_amax, d_scale_inv);
+    } else {
+        const int64_t blocks = stream_grid(n, kThreads, 8);
+        scaled_cast_scalar_kernel<SRC, FP8><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, d_amax,
+                                                                                             d_scale_inv, compat);
+    }
+}
+
+template <int SRC>
+void cast_dispatch_fp8(int fp8_dtype, const void* src, void* dst, int64_t n, const float* d_amax,
+                       float* d_scale_inv, int compat, cudaStream_t s) {
+    if (fp8_dtype == MF_DT_F8E4M3) cast_dispatch<SRC, MF_DT_F8E4M3>(src, dst, n, d_amax, d_scale_inv, compat, s);
+    else cast_dispatch<SRC, MF_DT_F8E5M2>(src, dst, n, d_amax, d_scale_inv, compat, s);
+}
+
+// ----------------------------------------------------- grouped (ckpt)
+
+constexpr int kGroupMaxChunks = 512;
+constexpr int kTileChunks = 4;                            // 16-element chunks per thread per tile
+constexpr int64_t kTileElems = int64_t(kThreads) * kTileChunks * kChunk;  // 16384
+
+struct ChunkRec {
+    const void* src;
+    void* dst;
+    int64_t n;
+    int64_t tile_begin;  // first global tile of this chunk
+    int32_t tensor;
+    int32_t flags;       // bit 0: 16-byte aligned src and dst; bits 8..15: src dtype
+};
+
+struct GroupArgs {
+    float* amax;
+    float* scale_inv;
+    int64_t total_tiles;
+    int32_t n_chunks;
+    int32_t fp8_dtype;
+    ChunkRec chunk[kGroupMaxChunks];
+};
+
+__device__ __forceinline__ int find_chunk(const GroupArgs& a, int64_t t) {
+    int lo = 0, hi = a.n_chunks - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.chunk[mid].tile_begin <= t) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// Running max of one tile of one chunk, by the chunk's source dtype.
+template <int SRC>
+__device__ __forceinline__ float tile_amax(const ChunkRec& ch, int64_t tile) {
+    const int64_t c0 = tile * (kTileElems / kChunk);
+    const int64_t full = ch.n / kChunk;
+    uint32_t key = 0;
+    float m = 0.0f;
+    if (ch.flags & 1) {
+        RawChunk<dtype_bytes(SRC)> r[kTileChunks];
+#pragma unroll
+        for (int k = 0; k < kTileChunks; ++k) {
+            const int64_t c = c0 + k * kThreads + threadIdx.x;
+            if (c < full) load_raw<dtype_bytes(SRC)>(ch.src, c, r[k]);
+        }
+#pragma unroll
+        for (int k = 0; k < kTileChunks; ++k) {
+            const int64_t c = c0 + k * kThreads + threadIdx.x;
+            if (c < full) key = MagKey<SRC>::fold(r[k], key);
+        }
+        m = MagKey<SRC>::to_f32(key);
+        // ragged end of the chunk: the last n mod 16 elements
+        const int64_t last_tile = (ch.n - 1) / kTileElems;
+        if (tile == last_tile && threadIdx.x < (ch.n % kChunk)) m = fmaxf(m, abs_or_zero<SRC>(ch.src, full * kChunk + threadIdx.x));
+    } else {
+        const int64_t e0 = tile * kTileElems;
+        for (int64_t i = e0 + threadIdx.x; i < e0 + kTileElems && i < ch.n; i += kThreads)
+            m = fmaxf(m, abs_or_zero<SRC>(ch.src, i));
+    }
+    return m;
+}
+
+template <int SRC, int FP8, int COMPAT>
+__device__ __forceinline__ void tile_cast(const ChunkRec& ch, int64_t tile, float scale) {
+    const int64_t c0 = tile * (kTileElems / kChunk);
+    const int64_t full = ch.n / kChunk;
+    if (ch.flags & 1) {
+        RawChunk<dtype_bytes(SRC)> r[kTileChunks];
+#pragma unroll
+        for (int k = 0; k < kTileChunks; ++k) {
+            const int64_t c = c0 + k * kThreads + threadIdx.x;
+            if (c < full) load_raw<dtype_bytes(SRC)>(ch.src, c, r[k]);
+        }
+#pragma unroll
+        for (int k = 0; k < kTileChunks; ++k) {
+            const int64_t c = c0 + k * kThreads + threadIdx.x;
+            if (c < full) {
+                float v[kChunk];
+                decode16<SRC>(r[k], v);
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) v[j] = __fmul_rn(v[j], scale);
+                RawChunk<1> o;
+                encode16<FP8>(v, o, COMPAT);
+                store_raw<1>(ch.dst, c, o);
+            }
+        }
+        const int64_t last_tile = (ch.n - 1) / kTileElems;
+        if (tile == last_tile && threadIdx.x < (ch.n % kChunk)) {
+            const int64_t i = full * kChunk + threadIdx.x;
+            store_code<FP8>(ch.dst, i, encode_fp8<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), scale), COMPAT));
+        }
+    } else {
+        const int64_t e0 = tile * kTileElems;
+        for (int64_t i = e0 + threadIdx.x; i < e0 + kTileElems && i < ch.n; i += kThreads)
+            store_code<FP8>(ch.dst, i, encode_fp8<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), scale), COMPAT));
+    }
+}
+
+__device__ __forceinline__ int chunk_dtype(const ChunkRec& ch) { return (ch.flags >> 8) & 0xff; }
+
+// This CTA's contiguous tile range [t0, t1).
+__device__ __forceinline__ void tile_range(int64_t total, int64_t& t0, int64_t& t1) {
+    const int64_t per = total / gridDim.x, extra = total % gridDim.x;
+    const int64_t b = blockIdx.x;
+    t0 = b * per + (b < extra ? b : extra);
+    t1 = t0 + per + (b < extra ? 1 : 0);
+}
+
+__global__ void __launch_bounds__(kThreads) group_amax_kernel(const __grid_constant__ GroupArgs a) {
+    int64_t t0, t1;
+    tile_range(a.total_tiles, t0, t1);
+    if (t0 >= t1) return;
+    int k = find_chunk(a, t0);
+    float m = 0.0f;
+    for (int64_t t = t0; t < t1; ++t) {
+        while (k + 1 < a.n_chunks && t >= a.chunk[k + 1].tile_begin) {
+            const float bm = block_max(m);
+            if (threadIdx.x == 0) atomic_max_nonneg(a.amax + a.chunk[k].tensor, bm);
+            m = 0.0f;
+            ++k;
+        }
+        const ChunkRec& ch = a.chunk[k];
+        const int64_t tile = t - ch.tile_begin;
+        switch (chunk_dtype(ch)) {
+        case MF_DT_BF16: m = fmaxf(m, tile_amax<MF_DT_BF16>(ch, tile)); break;
+        case MF_DT_F16: m = fmaxf(m, tile_amax<MF_DT_F16>(ch, tile)); break;
+        default: m = fmaxf(m, tile_amax<MF_DT_F32>(ch, tile)); break;
+        }
+    }
+    const float bm = block_max(m);
+    if (threadIdx.x == 0) atomic_max_nonneg(a.amax + a.chunk[k].tensor, bm);
+}
+
+template <int FP8, int COMPAT>
+__global__ void __launch_bounds__(kThreads) group_cast_kernel(const __grid_constant__ GroupArgs a) {
+    int64_t t0, t1;
+    tile_range(a.total_tiles, t0, t1);
+    if (t0 >= t1) return;
+    int k = find_chunk(a, t0);
+    float scale = scale_from_amax(a.amax[a.chunk[k].tensor], FP8);
+    for (int64_t t = t0; t < t1; ++t) {
+        while (k + 1 < a.n_chunks && t >= a.chunk[k + 1].tile_begin) {
+            ++k;
+            scale = scale_from_amax(a.amax[a.chunk[k].tensor], FP8);
+        }
+        const ChunkRec& ch = a.chunk[k];
+        const int64_t tile = t - ch.tile_begin;
+        if (tile == 0 && threadIdx.x == 0 && a.scale_inv)
+            a.scale_inv[ch.tensor] = scale_inv_from_amax(a.amax[ch.tensor], FP8);
+        switch (chunk_dtype(ch)) {
+        case MF_DT_BF16: tile_cast<MF_DT_BF16, FP8, COMPAT>(ch, tile, scale); break;
+        case MF_DT_F16: tile_cast<MF_DT_F16, FP8, COMPAT>(ch, tile, scale); break;
+        default: tile_cast<MF_DT_F32, FP8, COMPAT>(ch, tile, scale); break;
+        }
+    }
+}
+
+// Fill `a` from chunks[first, first+count); returns the number of tiles.
+int64_t fill_group(GroupArgs& a, const mf_chunk_desc* chunks, int first, int count) {
+    int64_t tiles = 0;
+    int used = 0;
+    for (int i = 0; i < count; ++i) {
+        const mf_chunk_desc& d = chunks[first + i];
+        if (d.n <= 0) continue;
+        ChunkRec& r = a.chunk[used++];
+        r.src = d.src;
+        r.dst = d.dst;
+        r.n = d.n;
+        r.tile_begin = tiles;
+        r.tensor = d.tensor;
+        r.flags = ((aligned16(d.src) && aligned16(d.dst)) ? 1 : 0) | (d.src_dtype << 8);
+        tiles += (d.n + kTileElems - 1) / kTileElems;
+    }
+    a.n_chunks = used;
+    a.total_tiles = tiles;
+    return tiles;
+}
+
+}  // namespace
+
+int launch_amax(const void* src, int src_dtype, int64_t n, float* d_amax, cudaStream_t s) {
+    if (n == 0) return MF_OK;
+    switch (src_dtype) {
+    case MF_DT_F32: amax_dispatch<MF_DT_F32>(src, n, d_amax, s); break;
+    case MF_DT_F16: amax_dispatch<MF_DT_F16>(src, n, d_amax, s); break;
+    case MF_DT_BF16: amax_dispatch<MF_DT_BF16>(src, n, d_amax, s); break;
+    case MF_DT_F8E4M3: amax_dispatch<MF_DT_F8E4M3>(src, n, d_amax, s); break;
+    case MF_DT_F8E5M2: amax_dispatch<MF_DT_F8E5M2>(src, n, d_amax, s); break;
+    default: return fail(MF_ERR_DTYPE_UNSUPPORTED, "amax: source dtype %d unsupported", src_dtype);
+    }
+    MF_LAUNCH_CHECK("amax launch");
+    return MF_OK;
+}
+
+int launch_scaled_cast(const void* src, int src_dtype, void* dst, int fp8_dtype, const float* d_amax,
+                       float* d_scale_inv, int64_t n, int compat, cudaStream_t s) {
+    if (n == 0) return MF_OK;
+    switch (src_dtype) {
+    case MF_DT_F32: cast_dispatch_fp8<MF_DT_F32>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
+    case MF_DT_F16: cast_dispatch_fp8<MF_DT_F16>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
+    case MF_DT_BF16: cast_dispatch_fp8<MF_DT_BF16>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
+    default: return fail(MF_ERR_DTYPE_UNSUPPORTED, "scaled cast: source dtype %d unsupported", src_dtype);
+    }
+    MF_LAUNCH_CHECK("scaled cast launch");
+    return MF_OK;
+}
+
+}  // namespace mf
+
+using namespace mf;
+
+static int check_quant_args(const char* name, int src_dtype, int fp8_dtype, int compat, int64_t n) {
+    if (n < 0) return fail(MF_ERR_SHAPE_INVALID, "%s: negative element count %lld", name, (long long)n);
+    if (!is_fp8(fp8_dtype)) return fail(MF_ERR_DTYPE_UNSUPPORTED, "%s: destination dtype %d is not FP8", name, fp8_dtype);
+    if (!is_float_store_dtype(src_dtype))
+        return fail(MF_ERR_DTYPE_UNSUPPORTED, "%s: source dtype %d unsupported (F32, F16, BF16)", name, src_dtype);
+    if (compat != MF_COMPAT_REFERENCE && compat != MF_COMPAT_OCP)
+        return fail(MF_ERR_INVALID_ARGUMENT, "%s: unknown compat mode %d", name, compat);
+    return MF_OK;
+}
+
+extern "C" int mf_amax(const void* src, int src_dtype, int64_t n, float* d_amax, mf_stream stream) {
+    MF_ENTER();
+    if (n < 0) return fail(MF_ERR_SHAPE_INVALID, "mf_amax: negative element count %lld", (long long)n);
+    if (!d_amax) return fail(MF_ERR_INVALID_ARGUMENT, "mf_amax: d_amax is NULL");
+    if (n > 0 && !src) return fail(MF_ERR_INVALID_ARGUMENT, "mf_amax: NULL source");
+    return launch_amax(src, src_dtype, n, d_amax, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mf_fp8_scaled_cast(const void* src, int src_dtype, void* dst, int fp8_dtype, const float* d_amax,
+                                  float* d_scale_inv, int64_t n, int compat, mf_stream stream) {
+    MF_ENTER();
+    int rc = check_quant_args("mf_fp8_scaled_cast", src_dtype, fp8_dtype, compat, n);
+    if (rc) return rc;
+    if (!d_amax) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fp8_scaled_cast: d_amax is NULL");
+    if (n > 0 && (!src || !dst)) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fp8_scaled_cast: NULL buffer");
+    if (n == 0) return MF_OK;
+    return launch_scaled_cast(src, src_dtype, dst, fp8_dtype, d_amax, d_scale_inv, n, compat,
+                              static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mf_fp8_quantize(const void* src, int src_dtype, void* dst, int fp8_dtype, float* d_amax,
+                               float* d_scale_inv, int64_t n, int compat, mf_stream stream) {
+    MF_ENTER();
+    int rc = check_quant_args("mf_fp8_quantize", src_dtype, fp8_dtype, compat, n);
+    if (rc) return rc;
+    if (!d_amax) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fp8_quantize: d_amax is NULL");
+    if (n > 0 && (!src || !dst)) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fp8_quantize: NULL buffer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    MF_CUDA_CHECK(cudaMemsetAsync(d_amax, 0, sizeof(float), s));
+    if (n == 0) return MF_OK;
+    rc = launch_amax(src, src_dtype, n, d_amax, s);
+    if (rc) return rc;
+    return launch_scaled_cast(src, src_dtype, dst, fp8_dtype, d_amax, d_scale_inv, n, compat, s);
+}
+
+extern "C" int mf_ckpt_partition(const int64_t* rows, int32_t n_tensors, int32_t world, int32_t rank,
+                                 int64_t* first_row, int64_t* n_rows) {
+    if (n_tensors < 0 || (n_tensors > 0 && (!rows || !first_row || !n_rows)))
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_partition: bad tensor table");
+    if (world < 1 || rank < 0 || rank >= world)
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_partition: rank %d outside world %d", rank, world);
+    for (int32_t t = 0; t < n_tensors; ++t) {
+        if (rows[t] < 0) return fail(MF_ERR_SHAPE_INVALID, "mf_ckpt_partition: tensor %d has %lld rows", t, (long long)rows[t]);
+        const int64_t base = rows[t] / world, extra = rows[t] % world;
+        first_row[t] = rank * base + (rank < extra ? rank : extra);
+        n_rows[t] = base + (rank < extra ? 1 : 0);
+    }
+    return MF_OK;
+}
+
+extern "C" int mf_ckpt_quant_fp8(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors, float* d_amax,
+                                 float* d_scale_inv, int fp8_dtype, int compat, mf_comm comm, mf_stream stream) {
+    MF_ENTER();
+    if (n_chunks < 0 || n_tensors <= 0 || (n_chunks > 0 && !chunks))
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8: bad chunk table (%d chunks, %d tensors)", n_chunks,
+                    n_tensors);
+    if (!d_amax) return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8: d_amax is NULL");
+    if (!is_fp8(fp8_dtype)) return fail(MF_ERR_DTYPE_UNSUPPORTED, "mf_ckpt_quant_fp8: dtype %d is not FP8", fp8_dtype);
+    if (compat != MF_COMPAT_REFERENCE && compat != MF_COMPAT_OCP)
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8: unknown compat mode %d", compat);
+    for (int32_t i = 0; i < n_chunks; ++i) {
+        const mf_chunk_desc& d = chunks[i];
+        if (d.tensor < 0 || d.tensor >= n_tensors)
+            return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8: chunk %d names tensor %d of %d", i, d.tensor, n_tensors);
+        if (d.n < 0) return fail(MF_ERR_SHAPE_INVALID, "mf_ckpt_quant_fp8: chunk %d has %lld elements", i, (long long)d.n);
+        if (!is_float_store_dtype(d.src_dtype))
+            return fail(MF_ERR_DTYPE_UNSUPPORTED, "mf_ckpt_quant_fp8: chunk %d source dtype %d unsupported", i, d.src_dtype);
+        if (d.n > 0 && (!d.src || !d.dst)) return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8: chunk %d has a NULL buffer", i);
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    MF_CUDA_CHECK(cudaMemsetAsync(d_amax, 0, sizeof(float) * n_tensors, s));
+    static GroupArgs args;  // large; filled and consumed by value at launch on this thread
+    static std::mutex args_mutex;
+    std::lock_guard<std::mutex> lock(args_mutex);
+    const int grid_cap = state().sm_count * 8;
+    for (int32_t first = 0; first < n_chunks; first += kGroupMaxChunks) {
+        const int count = std::min<int32_t>(kGroupMaxChunks, n_chunks - first);
+        args.amax = d_amax;
+        args.scale_inv = d_scale_inv;
+        args.fp8_dtype = fp8_dtype;
+        const int64_t tiles = fill_group(args, chunks, first, count);
+        if (tiles == 0) continue;
+        const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, grid_cap));
+        group_amax_kernel<<<blocks, kThreads, 0, s>>>(args);
+        MF_LAUNCH_CHECK("mf_ckpt_quant_fp8 amax launch");
+    }
+    if (comm) {
+        int rc = comm_allreduce_max(comm, d_amax, n_tensors, s);
+        if (rc) return rc;
+    }
+    for (int32_t first = 0; first < n_chunks; first += kGroupMaxChunks) {
+        const int count = std::min<int32_t>(kGroupMaxChunks, n_chunks - first);
+        args.amax = d_amax;
+        args.scale_inv = d_scale_inv;
+        args.fp8_dtype = fp8_dtype;
+        const int64_t tiles = fill_group(args, chunks, first, count);
+        if (tiles == 0) continue;
+        const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, grid_cap));
+        if (fp8_dtype == MF_DT_F8E4M3) {
+            if (compat) group_cast_kernel<MF_DT_F8E4M3, 1><<<blocks, kThreads, 0, s>>>(args);
+            else group_cast_kernel<MF_DT_F8E4M3, 0><<<blocks, kThreads, 0, s>>>(args);
+        } else {
+            if (compat) group_cast_kernel<MF_DT_F8E5M2, 1><<<blocks, kThreads, 0, s>>>(args);
+            else group_cast_kernel<MF_DT_F8E5M2, 0><<<blocks, kThreads, 0, s>>>(args);
+        }
+        MF_LAUNCH_CHECK("mf_ckpt_quant_fp8 cast launch");
+    }
+    return MF_OK;
+}

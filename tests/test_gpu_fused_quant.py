@@ -1,0 +1,313 @@
+"""K7 fused chains, K8 amax-scaled FP8 cast and K9 checkpoint quantisation on the GPU."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from manifesto_b200 import checkpoint, fusion, synthetic
+from manifesto_b200._abi import call, lib
+from manifesto_b200.dtype import DType
+from manifesto_b200.fusion import NodeType as N
+from oracle.ref import BF16, E4M3, E5M2, F16, F32, ITEMSIZE
+
+from .conftest import host_threads
+from .gpu_util import bits_equal, empty, fetch, to_device
+
+pytestmark = pytest.mark.gpu
+
+
+def ulp_diff_f32(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """|a - b| in float32 ulps (ordered integer distance; NaN == NaN)."""
+    ia = a.view(np.int32).astype(np.int64)
+    ib = b.view(np.int32).astype(np.int64)
+    oa = np.where(ia < 0, -(ia & 0x7FFFFFFF), ia)
+    ob = np.where(ib < 0, -(ib & 0x7FFFFFFF), ib)
+    d = np.abs(oa - ob)
+    both_nan = np.isnan(a.view(np.float32)) & np.isnan(b.view(np.float32))
+    return np.where(both_nan, 0, d)
+
+
+def ulp_diff_16(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    ia = a.astype(np.int64)
+    ib = b.astype(np.int64)
+    oa = np.where(ia & 0x8000, -(ia & 0x7FFF), ia)
+    ob = np.where(ib & 0x8000, -(ib & 0x7FFF), ib)
+    return np.abs(oa - ob)
+
+
+def ulp_diff_fp8(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Distance in FP8 codes between sign-magnitude codes (adjacent values differ by 1)."""
+    ia = a.astype(np.int64)
+    ib = b.astype(np.int64)
+    oa = np.where(ia & 0x80, -(ia & 0x7F), ia)
+    ob = np.where(ib & 0x80, -(ib & 0x7F), ib)
+    return np.abs(oa - ob)
+
+
+def run_fused(k: fusion.CUDAKernel, inputs, n, out_dt, amax=False):
+    bufs = [to_device(a) for a in inputs]
+    d = empty(n * ITEMSIZE[out_dt] + 64)
+    am = empty(4, fill=0) if amax else None
+    k.run([b.ptr for b in bufs], d.ptr, n, amax=am.ptr if am else None)
+    out = fetch(d, n * ITEMSIZE[out_dt] + 64)
+    assert (out[n * ITEMSIZE[out_dt]:] == 0xA5).all()
+    amv = float(fetch(am, 4, np.float32)[0]) if amax else None
+    for b in bufs + [d] + ([am] if am else []):
+        b.free()
+    return out[: n * ITEMSIZE[out_dt]].view({2: np.uint16, 4: np.uint32}[ITEMSIZE[out_dt]]), amv
+
+
+def test_relu_add_known_answer(backend, golden):
+    case = golden["known_answers"]["fused_relu_add"]
+    root = fusion.unary(N.RELU, fusion.binary(N.ADD, fusion.input_node(0), fusion.input_node(1)))
+    k = fusion.emit_cuda(fusion.FusionAST(root, ["x", "y"], "result"))
+    assert k.identifier() == "result" and k.target() == fusion.Target.CUDA
+    out, _ = run_fused(k, [np.array(case["x"], np.float32), np.array(case["y"], np.float32)], 4, F32)
+    assert out.view(np.float32).tolist() == case["out"]
+    with pytest.raises(Exception, match="expects 2 inputs"):
+        k.run([1], 1, 2)
+
+
+@pytest.mark.parametrize("op", [N.SIGMOID, N.TANH, N.GELU, N.SILU, N.EXP, N.LOG, N.SQRT])
+def test_activations_within_2ulp(backend, ref, op):
+    n = 1 << 16
+    x = synthetic.normal_f32(int(op), n, 0.0, 4.0)
+    if op in (N.LOG, N.SQRT):
+        x = np.abs(x)
+    x[:4] = [0.0, 1.0, -1.0, 2.0]
+    root = fusion.unary(op, fusion.input_node(0))
+    f = fusion.FusionAST(root, ["x"], "o")
+    k = fusion.emit_cuda(f)
+    got, _ = run_fused(k, [x], n, F32)
+    want = ref.fused_eval(fusion.node_table(root), [x], [F32], [0], F32, n)
+    assert ulp_diff_f32(got, want).max() <= 2
+
+
+def random_tree(rng, depth, n_inputs):
+    if depth == 0 or rng.random() < 0.25:
+        if rng.random() < 0.8:
+            return fusion.input_node(int(rng.integers(n_inputs)))
+        return fusion.constant_node(float(rng.normal()))
+    if rng.random() < 0.5:
+        op = N(int(rng.integers(int(N.ADD), int(N.MIN) + 1)))
+        return fusion.binary(op, random_tree(rng, depth - 1, n_inputs), random_tree(rng, depth - 1, n_inputs))
+    op = N(int(rng.integers(int(N.NEG), int(N.LEAKY_RELU) + 1)))
+    return fusion.unary(op, random_tree(rng, depth - 1, n_inputs))
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_random_chains_f32(backend, ref, seed):
+    rng = np.random.default_rng(seed)
+    n_in = 3
+    root = random_tree(rng, 4, n_in)
+    n = 20000
+    ins = [synthetic.normal_f32(seed * 10 + j, n) for j in range(n_in)]
+    bc = [0, 0, 0]
+    if seed % 3 == 0:
+        bc[2] = 100
+    k = fusion.emit_cuda(fusion.FusionAST(root, ["a", "b", "c"], "o"), in_bcast=bc)
+    got, _ = run_fused(k, ins, n, F32)
+    want = ref.fused_eval(fusion.node_table(root), ins, [F32] * n_in, bc, F32, n)
+    assert ulp_diff_f32(got, want).max() <= 2
+
+
+@pytest.mark.parametrize("out_dt", [BF16, F16])
+def test_random_chains_16bit_io(backend, ref, out_dt):
+    rng = np.random.default_rng(77)
+    root = random_tree(rng, 4, 2)
+    n = 30000
+    ins = [synthetic.normal_bf16(5, n), synthetic.normal_f32(6, n).astype(np.float16).view(np.uint16)]
+    k = fusion.emit_cuda(fusion.FusionAST(root, ["a", "b"], "o"), in_dtypes=[DType.BFLOAT16, DType.FLOAT16],
+                         out_dtype=DType(out_dt))
+    got, _ = run_fused(k, ins, n, out_dt)
+    want = ref.fused_eval(fusion.node_table(root), ins, [BF16, F16], [0, 0], out_dt, n)
+    assert ulp_diff_16(got, want).max() <= 1
+
+
+def swiglu_inputs(n, hidden=4096, seed=synthetic.CONFIG_SEED + 40):
+    x = synthetic.normal_bf16(seed, n)
+    y = synthetic.normal_bf16(seed + 1, n)
+    g = synthetic.normal_bf16(seed + 2, hidden, 1.0, 0.1)
+    b = synthetic.normal_bf16(seed + 3, hidden, 0.0, 0.1)
+    return [x, g, b, y]
+
+
+def swiglu_kernel(hidden=4096):
+    f = fusion.swiglu_chain()
+    return f, fusion.emit_cuda(f, in_dtypes=[DType.BFLOAT16] * 4, in_bcast=[0, hidden, hidden, 0],
+                               out_dtype=DType.BFLOAT16)
+
+
+def test_swiglu_specialised_within_1ulp(backend, ref):
+    n = 64 * 4096 * 4
+    f, k = swiglu_kernel()
+    assert k.specialised()
+    ins = swiglu_inputs(n)
+    got, amax = run_fused(k, ins, n, BF16, amax=True)
+    want = ref.fused_eval(fusion.node_table(f.root), ins, [BF16] * 4, [0, 4096, 4096, 0], BF16, n,
+                          threads=host_threads())
+    d = ulp_diff_16(got, want)
+    assert d.max() <= 1
+    # amax folds |BF16 output| exactly
+    assert amax == float(np.abs((got.astype(np.uint32) << 16).view(np.float32)).max())
+
+
+def test_swiglu_commuted_forms_specialise(backend):
+    x, g, b, y = (fusion.input_node(i, DType.BFLOAT16) for i in range(4))
+    root = fusion.binary(N.MUL, y, fusion.unary(N.SILU, fusion.binary(N.ADD, b, fusion.binary(N.MUL, g, x))))
+    k = fusion.emit_cuda(fusion.FusionAST(root, ["x", "g", "b", "y"], "o", dtype=DType.BFLOAT16),
+                         in_bcast=[0, 4096, 4096, 0])
+    assert k.specialised()
+    k2 = fusion.emit_cuda(fusion.FusionAST(root, ["x", "g", "b", "y"], "o", dtype=DType.BFLOAT16))
+    assert not k2.specialised()  # no broadcast inputs -> interpreter
+
+
+def test_fused_fp8_pipeline(backend, ref):
+    """Config 4 at reduced size: chain -> BF16 -> amax -> E4M3, within 1 FP8 code."""
+    n = 8 * 2048 * 4096 // 8
+    f, k = swiglu_kernel()
+    ins = swiglu_inputs(n)
+    bufs = [to_device(a) for a in ins]
+    pre = empty(n * 2)
+    q = empty(n)
+    am = empty(4)
+    si = empty(4)
+    k.run_fp8([b.ptr for b in bufs], pre.ptr, q.ptr, n, am.ptr, si.ptr)
+    got_pre = fetch(pre, n * 2, np.uint16)
+    got_q = fetch(q, n)
+    got_amax = float(fetch(am, 4, np.float32)[0])
+    got_si = float(fetch(si, 4, np.float32)[0])
+    want_pre = ref.fused_eval(fusion.node_table(f.root), ins, [BF16] * 4, [0, 4096, 4096, 0], BF16, n,
+                              threads=host_threads())
+    assert ulp_diff_16(got_pre, want_pre).max() <= 1
+    want_amax = ref.amax(want_pre, BF16)
+    want_q = ref.scaled_cast(want_pre, BF16, E4M3, want_amax, threads=host_threads())
+    assert ulp_diff_fp8(got_q, want_q).max() <= 1
+    # the GPU's own precast -> its FP8 output is bit-exact under the oracle's cast
+    bits_equal(got_q, ref.scaled_cast(got_pre, BF16, E4M3, got_amax, threads=host_threads()))
+    assert got_amax == ref.amax(got_pre, BF16)
+    assert got_si == ref.fp8_scale_inv(got_amax, E4M3)
+    for b in bufs + [pre, q, am, si]:
+        b.free()
+
+
+# --------------------------------------------------------------- quant
+
+@pytest.mark.parametrize("dt", [F32, BF16, F16, E4M3, E5M2])
+def test_amax(backend, ref, dt):
+    n = 100003
+    raw = synthetic.uniform_bytes(dt, n * ITEMSIZE[dt])
+    d = to_device(raw)
+    am = empty(4, fill=0)
+    call("mf_amax", d.ptr, dt, n, am.ptr, None)
+    got = float(fetch(am, 4, np.float32)[0])
+    assert got == ref.amax(raw, dt)
+    d.free()
+    am.free()
+
+
+@pytest.mark.parametrize("src", [F32, BF16, F16])
+@pytest.mark.parametrize("fp8", [E4M3, E5M2])
+@pytest.mark.parametrize("compat", [0, 1])
+def test_fp8_quantize_bit_exact(backend, ref, src, fp8, compat):
+    n = (1 << 20) + 7
+    if src == F32:
+        raw = synthetic.normal_f32(src, n, 0, 2.0)
+    elif src == BF16:
+        raw = synthetic.normal_bf16(src, n, 0, 2.0)
+    else:
+        raw = synthetic.normal_f32(src, n, 0, 2.0).astype(np.float16).view(np.uint16)
+    raw[5] = {F32: 0x7FC00000, BF16: 0x7FC0, F16: 0x7E00}[src]  # a NaN is ignored by amax
+    d = to_device(raw)
+    q = empty(n)
+    am = empty(4)
+    si = empty(4)
+    call("mf_fp8_quantize", d.ptr, src, q.ptr, fp8, am.ptr, si.ptr, n, compat, None)
+    got_amax = float(fetch(am, 4, np.float32)[0])
+    assert got_amax == ref.amax(raw, src)
+    bits_equal(fetch(q, n), ref.scaled_cast(raw, src, fp8, got_amax, compat))
+    assert float(fetch(si, 4, np.float32)[0]) == ref.fp8_scale_inv(got_amax, fp8)
+    for b in (d, q, am, si):
+        b.free()
+
+
+def test_quantize_zero_and_tiny(backend, ref):
+    n = 4096
+    raw = np.zeros(n, np.uint16)
+    raw[7] = 0x0001  # BF16 subnormal
+    d = to_device(raw)
+    q = empty(n)
+    am = empty(4)
+    call("mf_fp8_quantize", d.ptr, BF16, q.ptr, E4M3, am.ptr, None, n, 0, None)
+    got_amax = float(fetch(am, 4, np.float32)[0])
+    bits_equal(fetch(q, n), ref.scaled_cast(raw, BF16, E4M3, got_amax))
+    raw[:] = 0
+    d.upload(raw)
+    call("mf_fp8_quantize", d.ptr, BF16, q.ptr, E4M3, am.ptr, None, n, 0, None)
+    assert float(fetch(am, 4, np.float32)[0]) == 0.0
+    assert (fetch(q, n) == 0).all()
+    for b in (d, q, am):
+        b.free()
+
+
+# -------------------------------------------------------- checkpoint
+
+def small_layout():
+    return checkpoint.llama3_8b_layout(layers=2, hidden=512, mlp=1792, heads=8, kv_heads=2, vocab=4000)
+
+
+@pytest.mark.parametrize("world", [1, 3, 8])
+def test_ckpt_sharded_emulated_bit_exact(backend, ref, world):
+    """All ranks' chunks in one grouped launch (the ranks emulated on one GPU)."""
+    specs = small_layout()
+    host = [synthetic.normal_bf16(1000 + i, s.numel, 0.0, 0.02) for i, s in enumerate(specs)]
+    srcs = [to_device(h) for h in host]
+    dsts = [empty(s.numel) for s in specs]
+    entries = []
+    for r in range(world):
+        for t, ((first, rows), s) in enumerate(zip(checkpoint.partition(specs, world, r), specs)):
+            off = first * s.cols
+            entries.append((srcs[t].ptr + 2 * off, dsts[t].ptr + off, rows * s.cols, t, DType.BFLOAT16))
+    chunks = checkpoint.make_chunks(entries)
+    am = empty(4 * len(specs))
+    si = empty(4 * len(specs))
+    checkpoint.quantise(chunks, len(entries), len(specs), am.ptr, si.ptr)
+    amax = fetch(am, 4 * len(specs), np.float32)
+    sinv = fetch(si, 4 * len(specs), np.float32)
+    for t, h in enumerate(host):
+        want_amax = ref.amax(h, BF16)
+        assert amax[t] == want_amax, specs[t].name
+        assert sinv[t] == ref.fp8_scale_inv(want_amax, E4M3)
+        bits_equal(fetch(dsts[t], specs[t].numel), ref.scaled_cast(h, BF16, E4M3, want_amax))
+    for b in srcs + dsts + [am, si]:
+        b.free()
+
+
+def test_ckpt_many_chunks_and_ragged(backend, ref):
+    """More chunks than one launch holds, ragged sizes and unaligned chunk starts."""
+    rng = np.random.default_rng(5)
+    sizes = [int(v) for v in rng.integers(1, 40000, size=700)]
+    host = [synthetic.normal_bf16(i, s, 0, 1.0) for i, s in enumerate(sizes)]
+    srcs = [to_device(h, pad=32) for h in host]
+    dsts = [empty(s + 32) for s in sizes]
+    entries = []
+    for t, s in enumerate(sizes):
+        off = t % 3  # unaligned starts for some chunks
+        entries.append((srcs[t].ptr + 2 * off, dsts[t].ptr + off, s - off, t, DType.BFLOAT16))
+    am = empty(4 * len(sizes))
+    checkpoint.quantise(checkpoint.make_chunks(entries), len(entries), len(sizes), am.ptr, None)
+    amax = fetch(am, 4 * len(sizes), np.float32)
+    for t, s in enumerate(sizes):
+        off = t % 3
+        h = host[t][off:]
+        assert amax[t] == ref.amax(h, BF16)
+        bits_equal(fetch(dsts[t], s - off, offset=off), ref.scaled_cast(h, BF16, E4M3, float(amax[t])))
+    for b in srcs + dsts + [am]:
+        b.free()
+
+
+def test_ckpt_rejects(backend):
+    arr = checkpoint.make_chunks([(1, 1, 10, 5, DType.BFLOAT16)])
+    assert lib().mf_ckpt_quant_fp8(arr, 1, 2, 1, None, E4M3, 0, None, None) == -1  # tensor 5 of 2
+    arr = checkpoint.make_chunks([(1, 1, 10, 0, DType.FLOAT8_E4M3)])
+    assert lib().mf_ckpt_quant_fp8(arr, 1, 1, 1, None, E4M3, 0, None, None) == -3

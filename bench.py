@@ -1,0 +1,535 @@
+#!/usr/bin/env python
+"""Benchmark of manifesto's dtype/convert + fused-elementwise hot path on B200.
+
+Headline workload (one JSON line on rank 0): whole-checkpoint FP8 E4M3
+quantisation of a Llama-3-8B layout (291 BF16 tensors, 8,030,261,248 params,
+values N(0, 0.02)) with per-tensor amax scales, every tensor row-split over the
+N ranks (strong scaling: the checkpoint is fixed), one NCCL max all-reduce of the
+amax vector per step.  A step = pass 1 (amax) + all-reduce + pass 2 (cast)
+through the C ABI (mf_ckpt_quant_fp8).
+
+  value      params quantised per second, whole job (max-over-ranks device time)
+  e2e        the same through the C ABI with host buffers: pinned host BF16 ->
+             device, quantise, FP8 + scales -> host, every step
+  roofline   the dominant kernel (pass 2, group_cast_kernel) timed alone with
+             CUDA events: 3 B/param (read BF16, write FP8) / launch time vs the
+             measured HBM copy peak
+  kernels    (N=1) every other benchmark config as its own kernel line: FP8->FP32
+             decode, Int4 group dequant, axpy f32/bf16, fused SwiGLU->FP8
+  cpu_baseline  (N=1, rank 0) the C oracle port of the Go loops on the host cores,
+             on a bounded sample (decoder layer 0: 218,112,000 params)
+
+--impl reference times that CPU port alone (the reference is Go; no Go toolchain
+exists on these machines, so the port stands in for it).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "achieved HBM GB/s and % of 8 TB/s roofline per kernel; elems/s at 1/2/4/8 B200"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+E4M3 = 5
+BF16 = 4
+F32 = 2
+
+
+def hbm_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_table() -> dict:
+    """Per-unit DRAM bytes measured with ncu (profiles/traffic.txt: kernel bytes_per_elem)."""
+    out = {}
+    p = ROOT / "profiles" / "traffic.txt"
+    if p.exists():
+        for line in p.read_text().splitlines():
+            parts = line.split()
+            if len(parts) >= 2 and not line.startswith("#"):
+                try:
+                    out[parts[0]] = float(parts[1])
+                except ValueError:
+                    pass
+    return out
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU's clocks during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------- our arm
+
+class Dist:
+    def __init__(self, world: int, rank: int, local_rank: int):
+        self.world, self.rank, self.local_rank = world, rank, local_rank
+        self.pg = None
+
+    def init(self, torch) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                    device_id=torch.device("cuda", self.local_rank))
+            self.pg = dist
+
+    def barrier(self, torch) -> None:
+        if self.pg:
+            self.pg.barrier()
+        torch.cuda.synchronize()
+
+    def max(self, torch, v: float) -> float:
+        if not self.pg:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def broadcast_bytes(self, data: bytes | None) -> bytes:
+        if not self.pg:
+            return data
+        obj = [data]
+        self.pg.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def close(self) -> None:
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def fill_normal_bf16(torch, t, seed: int, mu: float, sigma: float, chunk: int = 1 << 27) -> None:
+    """Fill a bf16 tensor with N(mu, sigma) from a seeded device generator."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    flat = t.view(-1)
+    for b in range(0, flat.numel(), chunk):
+        e = min(flat.numel(), b + chunk)
+        flat[b:e].copy_((torch.randn(e - b, device="cuda", generator=g) * sigma + mu).to(torch.bfloat16))
+
+
+def time_launches(torch, fn, reps: int, flush=None) -> list[float]:
+    """Per-launch device times (ms) with CUDA events on torch's current stream."""
+    out = []
+    for _ in range(reps):
+        if flush is not None:
+            flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        out.append(s.elapsed_time(e))
+    return out
+
+
+def kernel_line(name: str, alg_bytes: float, times_ms: list[float], peak: float, elems: int) -> dict:
+    ms = statistics.median(times_ms)
+    gbs = alg_bytes / (ms * 1e-3) / 1e9
+    return {"kernel": name, "ms": round(ms, 4), "alg_bytes": int(alg_bytes), "gbs": round(gbs, 1),
+            "frac_of_measured": round(gbs / peak, 4), "frac_of_8tbs": round(gbs / NOMINAL_HBM_GBS, 4),
+            "elems_per_s": elems / (ms * 1e-3), "reps": len(times_ms)}
+
+
+def bench_kernels(torch, stream_handle: int, peak: float) -> dict:
+    """Configs 1-4 on one GPU, each kernel timed alone with L2 flushed before every launch."""
+    from manifesto_b200 import fusion
+    from manifesto_b200._abi import call
+    from manifesto_b200.dtype import DType
+
+    flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+    flush = lambda: flush_buf.fill_(1)
+    out = {}
+    reps = 20
+
+    # config 1: FP8 E4M3 -> FP32, 2^26 elements (all 256 codes uniform)
+    n = 1 << 26
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
+    dst = torch.empty(n, dtype=torch.float32, device="cuda")
+    f = lambda: call("mf_convert", 5, 2, src.data_ptr(), dst.data_ptr(), n, 0, stream_handle)
+    for _ in range(3):
+        f()
+    out["c1_fp8e4m3_to_f32"] = kernel_line("convert_vec_kernel<E4M3,F32>", 5 * n, time_launches(torch, f, reps, flush),
+                                           peak, n)
+    del src, dst
+
+    # config 2: Int4 -> BF16 dequant, 4096 x 14336, group 128, BF16 scales ~ |N(0, 0.02)|
+    rows, cols, group = 4096, 14336, 128
+    q = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device="cuda")
+    sc = (torch.randn(rows * cols // group, device="cuda").abs() * 0.02).to(torch.bfloat16)
+    o = torch.empty(rows * cols, dtype=torch.bfloat16, device="cuda")
+    f = lambda: call("mf_int4_dequant_grouped", q.data_ptr(), sc.data_ptr(), 4, o.data_ptr(), 4, rows, cols, group,
+                     stream_handle)
+    for _ in range(3):
+        f()
+    b = rows * cols // 2 + sc.numel() * 2 + rows * cols * 2
+    out["c2_int4_to_bf16"] = kernel_line("int4_dequant_vec_kernel<BF16,BF16>", b, time_launches(torch, f, reps, flush),
+                                         peak, rows * cols)
+    del q, sc, o
+
+    # config 3: axpy f32 and bf16, N = 2^28, alpha = 0.75
+    n = 1 << 28
+    x = torch.randn(n, device="cuda")
+    y = torch.randn(n, device="cuda")
+    f = lambda: call("mf_axpy", y.data_ptr(), x.data_ptr(), n, 0.75, 2, 0, stream_handle)
+    for _ in range(3):
+        f()
+    out["c3a_axpy_f32"] = kernel_line("axpy_vec_kernel<F32>", 12 * n, time_launches(torch, f, reps, flush), peak, n)
+    xb, yb = x.to(torch.bfloat16), y.to(torch.bfloat16)
+    del x, y
+    f = lambda: call("mf_axpy", yb.data_ptr(), xb.data_ptr(), n, 0.75, 4, 0, stream_handle)
+    for _ in range(3):
+        f()
+    out["c3b_axpy_bf16"] = kernel_line("axpy_vec_kernel<BF16>", 6 * n, time_launches(torch, f, reps, flush), peak, n)
+    del xb, yb
+
+    # config 4: Mul(Silu(Add(Mul(x, gamma), beta)), y) on BF16 [64, 2048, 4096] -> amax -> E4M3
+    hidden = 4096
+    n = 64 * 2048 * hidden
+    x = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    fill_normal_bf16(torch, x, 41, 0.0, 1.0)
+    fill_normal_bf16(torch, y, 42, 0.0, 1.0)
+    g = (torch.randn(hidden, device="cuda") * 0.1 + 1.0).to(torch.bfloat16)
+    be = (torch.randn(hidden, device="cuda") * 0.1).to(torch.bfloat16)
+    pre = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    qo = torch.empty(n, dtype=torch.uint8, device="cuda")
+    am = torch.zeros(1, dtype=torch.float32, device="cuda")
+    si = torch.zeros(1, dtype=torch.float32, device="cuda")
+    k = fusion.emit_cuda(fusion.swiglu_chain(), in_dtypes=[DType.BFLOAT16] * 4, in_bcast=[0, hidden, hidden, 0],
+                         out_dtype=DType.BFLOAT16)
+    ptrs = [x.data_ptr(), g.data_ptr(), be.data_ptr(), y.data_ptr()]
+    f = lambda: k.run_fp8(ptrs, pre.data_ptr(), qo.data_ptr(), n, am.data_ptr(), si.data_ptr(), stream=stream_handle)
+    for _ in range(3):
+        f()
+    out["c4_fused_swiglu_fp8"] = kernel_line("swiglu_bf16_kernel + scaled_cast_vec_kernel", 9 * n,
+                                             time_launches(torch, f, max(5, reps // 2), flush), peak, n)
+    f1 = lambda: k.run(ptrs, pre.data_ptr(), n, amax=am.data_ptr(), stream=stream_handle)
+    out["c4_pass1_swiglu"] = kernel_line("swiglu_bf16_kernel<amax>", 6 * n, time_launches(torch, f1, reps // 2, flush),
+                                         peak, n)
+    f2 = lambda: call("mf_fp8_scaled_cast", pre.data_ptr(), 4, qo.data_ptr(), 5, am.data_ptr(), si.data_ptr(), n, 0,
+                      stream_handle)
+    out["c4_pass2_cast"] = kernel_line("scaled_cast_vec_kernel<BF16,E4M3>", 3 * n,
+                                       time_launches(torch, f2, reps // 2, flush), peak, n)
+    out["c4_fused_swiglu_fp8"]["single_pass_lower_bound_bytes"] = 5 * n
+    k.close()
+    del x, y, pre, qo, flush_buf
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_ours(args, world: int, rank: int, local_rank: int) -> None:
+    import torch
+
+    from manifesto_b200 import CUDABackend, checkpoint
+    from manifesto_b200._abi import call
+
+    torch.cuda.set_device(local_rank)
+    CUDABackend(local_rank)
+    dist = Dist(world, rank, local_rank)
+    dist.init(torch)
+    stream = torch.cuda.current_stream().cuda_stream
+    peak, peak_src = hbm_peak()
+
+    specs = checkpoint.llama3_8b_layout()
+    total_params = sum(s.numel for s in specs)
+    parts = checkpoint.partition(specs, world, rank)
+    local = [rows * s.cols for (first, rows), s in zip(parts, specs)]
+    local_params = sum(local)
+    src = torch.empty(local_params, dtype=torch.bfloat16, device="cuda")
+    dst = torch.empty(local_params, dtype=torch.uint8, device="cuda")
+    amax = torch.zeros(len(specs), dtype=torch.float32, device="cuda")
+    sinv = torch.zeros(len(specs), dtype=torch.float32, device="cuda")
+    entries, off = [], 0
+    for t, n in enumerate(local):
+        if n:
+            fill_normal_bf16(torch, src[off:off + n], 1000 * t + rank, 0.0, 0.02)
+        entries.append((src.data_ptr() + 2 * off, dst.data_ptr() + off, n, t, BF16))
+        off += n
+    chunks = checkpoint.make_chunks(entries)
+    comm = None
+    if world > 1:
+        uid = dist.broadcast_bytes(checkpoint.Communicator.unique_id() if rank == 0 else None)
+        comm = checkpoint.Communicator(world, rank, uid)
+
+    def step():
+        checkpoint.quantise(chunks, len(entries), len(specs), amax.data_ptr(), sinv.data_ptr(), E4M3, 0, comm,
+                            stream)
+
+    for _ in range(args.warmup):
+        step()
+    dist.barrier(torch)
+    gpu_id = "GPU-" + str(torch.cuda.get_device_properties(local_rank).uuid).replace("GPU-", "")
+    sampler = ClockSampler(gpu_id)
+    sampler.start()
+    dist.barrier(torch)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    dist.barrier(torch)
+    clocks = sampler.stop()
+    local_ms = t0.elapsed_time(t1)
+    ms = dist.max(torch, local_ms)
+    value = total_params * args.steps / (ms * 1e-3)
+    job_gbs = 5.0 * total_params * args.steps / (ms * 1e-3) / 1e9
+
+    # dominant kernel alone: pass 2 (group_cast_kernel), events around each launch
+    def cast_only():
+        call("mf_ckpt_cast_pass", chunks, len(entries), len(specs), amax.data_ptr(), sinv.data_ptr(), E4M3, 0,
+             stream)
+
+    def amax_only():
+        call("mf_ckpt_amax_pass", chunks, len(entries), len(specs), amax.data_ptr(), stream)
+
+    reps = 10
+    cast_ms = statistics.mean(time_launches(torch, cast_only, reps))
+    amax_ms = statistics.mean(time_launches(torch, amax_only, reps))
+    step()  # restore amax after the extra amax passes
+    torch.cuda.synchronize()
+    cast_bytes = 3.0 * local_params
+    achieved = cast_bytes / (cast_ms * 1e-3) / 1e9
+    traffic = traffic_table().get("group_cast_kernel")
+    roofline = {"bound": "hbm", "kernel": "group_cast_kernel (pass 2: read BF16, write E4M3)",
+                "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_src, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "frac_of_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
+                "traffic": int(traffic * local_params) if traffic else None,
+                "alg_bytes_per_launch": int(cast_bytes), "launch_ms": round(cast_ms, 4),
+                "amax_pass": {"launch_ms": round(amax_ms, 4),
+                              "gbs": round(2.0 * local_params / (amax_ms * 1e-3) / 1e9, 1)}}
+
+    # end to end through the C ABI with host buffers
+    e2e = bench_e2e(args, torch, dist, chunks, entries, specs, src, dst, amax, sinv, comm, stream, local_params,
+                    total_params)
+
+    kernels = None
+    cpu = None
+    if world == 1 and not args.no_kernels:
+        kernels = bench_kernels(torch, stream, peak)
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(steps=2, warmup=0)
+
+    if comm is not None:
+        comm.close()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "elems/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0, 0.02) BF16 weights)",
+            "config": {"workload": "ckpt_fp8_e4m3_llama3_8b",
+                       "description": "whole-checkpoint per-tensor amax-scaled FP8 E4M3 quantisation, Llama-3-8B "
+                                      "layout (291 BF16 tensors), rows split over ranks, NCCL max all-reduce of amax",
+                       "tensors": len(specs), "params": total_params, "src_dtype": "bf16", "dst_dtype": "fp8e4m3",
+                       "compat": "reference", "parallelism": f"rowsplit{world}",
+                       "l2": "inputs larger than L2 (BF16 shard of 16.06 GB / N per rank)"},
+            "hbm_gbs_job": round(job_gbs, 1), "alg_bytes_per_param": 5,
+            "roofline": roofline, "e2e": e2e, "clocks": clocks, "gpu_launches": 2 * args.steps,
+        }
+        if kernels:
+            line["kernels"] = kernels
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
+def bench_e2e(args, torch, dist, chunks, entries, specs, src, dst, amax, sinv, comm, stream, local_params,
+              total_params) -> dict:
+    """Host BF16 (pinned) -> device -> quantise -> FP8 + scale_inv -> host, every step."""
+    from manifesto_b200 import PinnedBuffer, checkpoint
+    from manifesto_b200._abi import call
+
+    h_src = PinnedBuffer(2 * local_params)
+    h_dst = PinnedBuffer(local_params)
+    h_si = PinnedBuffer(4 * len(specs))
+    # the host copy holds the same weights the device holds
+    call("mf_memcpy_d2h_async", h_src.ptr, src.data_ptr(), 2 * local_params, stream)
+    torch.cuda.synchronize()
+
+    def step():
+        call("mf_memcpy_h2d_async", src.data_ptr(), h_src.ptr, 2 * local_params, stream)
+        checkpoint.quantise(chunks, len(entries), len(specs), amax.data_ptr(), sinv.data_ptr(), E4M3, 0, comm,
+                            stream)
+        call("mf_memcpy_d2h_async", h_dst.ptr, dst.data_ptr(), local_params, stream)
+        call("mf_memcpy_d2h_async", h_si.ptr, sinv.data_ptr(), 4 * len(specs), stream)
+
+    steps = max(2, min(args.steps, args.e2e_steps))
+    step()
+    dist.barrier(torch)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = dist.max(torch, t0.elapsed_time(t1))
+    for b in (h_src, h_dst, h_si):
+        b.free()
+    return {"value": total_params * steps / (ms * 1e-3), "unit": "elems/s", "steps": steps,
+            "ms_per_step": ms / steps, "h2d_bytes_per_step": 2 * local_params,
+            "d2h_bytes_per_step": local_params + 4 * len(specs), "path": "C ABI (mf_memcpy_* + mf_ckpt_quant_fp8)"}
+
+
+# ------------------------------------------------------ CPU / reference
+
+CPU_SAMPLE = "decoder layer 0 of the Llama-3-8B layout: 9 BF16 tensors, 218,112,000 params, N(0, 0.02)"
+
+
+def cpu_sample():
+    import numpy as np
+
+    from manifesto_b200 import checkpoint, synthetic
+    specs = checkpoint.llama3_8b_layout()[1:10]
+    assert all(s.name.startswith("model.layers.0.") for s in specs)
+    return [synthetic.normal_bf16(2000 + i, s.numel, 0.0, 0.02) for i, s in enumerate(specs)]
+
+
+def cpu_step(tensors, threads: int) -> None:
+    from oracle import ref
+    for t in tensors:
+        a = ref.amax(t, ref.BF16, threads=threads)
+        ref.scaled_cast(t, ref.BF16, ref.E4M3, a, threads=threads)
+
+
+def cpu_baseline(steps: int, warmup: int, tensors=None) -> dict:
+    tensors = tensors if tensors is not None else cpu_sample()
+    threads = os.cpu_count() or 1
+    n = sum(int(t.size) for t in tensors)
+    for _ in range(warmup):
+        cpu_step(tensors, threads)
+    t = time.perf_counter()
+    for _ in range(steps):
+        cpu_step(tensors, threads)
+    dt = (time.perf_counter() - t) / steps
+    return {"value": n / dt, "unit": "elems/s", "cores": threads, "kind": "port", "sample": CPU_SAMPLE,
+            "s_per_step": dt, "cpu": cpu_model()}
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, world: int, rank: int) -> None:
+    if rank != 0:
+        return
+    from oracle import ref
+    ref.lib()
+    tensors = cpu_sample()
+    b = cpu_baseline(steps=args.steps, warmup=args.warmup, tensors=tensors)
+    line = {
+        "metric": METRIC, "value": b["value"], "unit": "elems/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": b["s_per_step"] * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0, 0.02) BF16 weights)",
+        "config": {"workload": "ckpt_fp8_e4m3_llama3_8b", "params": 8030261248, "src_dtype": "bf16",
+                   "dst_dtype": "fp8e4m3", "compat": "reference", "sample": CPU_SAMPLE},
+        "impl": "reference",
+        "cpu_baseline": {"value": b["value"], "unit": "elems/s", "cores": b["cores"], "kind": "port",
+                         "sample": CPU_SAMPLE, "cpu": b["cpu"]},
+        "e2e": {"value": b["value"], "unit": "elems/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "manifesto is Go and no Go toolchain exists here; this times the C restatement of its scalar "
+                "loops (oracle/mfref.c) with all host threads",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-kernels", action="store_true", help="skip the per-config kernel lines (N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world == 1 and args.gpus > 1:
+        print(f"--gpus {args.gpus} needs torchrun with {args.gpus} processes", file=sys.stderr)
+        return 2
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_ours(args, world, rank, local_rank)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

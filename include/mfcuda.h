@@ -309,6 +309,17 @@ int mf_comm_destroy(mf_comm comm);
 /* In-place max all-reduce of a float vector in device memory. */
 int mf_comm_allreduce_max_f32(mf_comm comm, float* d_vec, int64_t count, mf_stream stream);
 
+/* The two passes on their own, for callers that run the amax exchange with
+ * their own collective: pass 1 folds max|chunk| into d_amax[chunk.tensor]
+ * (atomic max; the caller zeroes d_amax first); pass 2 casts every chunk
+ * with the scale of d_amax[chunk.tensor] and writes d_scale_inv (if not
+ * NULL).  One grouped launch per 512 chunks each. */
+int mf_ckpt_amax_pass(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors,
+                      float* d_amax, mf_stream stream);
+int mf_ckpt_cast_pass(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors,
+                      const float* d_amax, float* d_scale_inv, int fp8_dtype, int compat,
+                      mf_stream stream);
+
 /* Quantise every chunk: pass 1 folds per-tensor amax of this rank's
  * chunks into d_amax[n_tensors] (zeroed by this call), then, if comm is
  * not NULL, an NCCL max all-reduce makes d_amax global, then pass 2 casts

@@ -555,49 +555,60 @@ extern "C" int mf_ckpt_partition(const int64_t* rows, int32_t n_tensors, int32_t
     return MF_OK;
 }
 
-extern "C" int mf_ckpt_quant_fp8(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors, float* d_amax,
-                                 float* d_scale_inv, int fp8_dtype, int compat, mf_comm comm, mf_stream stream) {
-    MF_ENTER();
+static int check_chunks(const char* name, const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors,
+                        const float* d_amax) {
     if (n_chunks < 0 || n_tensors <= 0 || (n_chunks > 0 && !chunks))
-        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8: bad chunk table (%d chunks, %d tensors)", n_chunks,
-                    n_tensors);
-    if (!d_amax) return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8: d_amax is NULL");
-    if (!is_fp8(fp8_dtype)) return fail(MF_ERR_DTYPE_UNSUPPORTED, "mf_ckpt_quant_fp8: dtype %d is not FP8", fp8_dtype);
-    if (compat != MF_COMPAT_REFERENCE && compat != MF_COMPAT_OCP)
-        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8: unknown compat mode %d", compat);
+        return fail(MF_ERR_INVALID_ARGUMENT, "%s: bad chunk table (%d chunks, %d tensors)", name, n_chunks, n_tensors);
+    if (!d_amax) return fail(MF_ERR_INVALID_ARGUMENT, "%s: d_amax is NULL", name);
     for (int32_t i = 0; i < n_chunks; ++i) {
         const mf_chunk_desc& d = chunks[i];
         if (d.tensor < 0 || d.tensor >= n_tensors)
-            return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8: chunk %d names tensor %d of %d", i, d.tensor, n_tensors);
-        if (d.n < 0) return fail(MF_ERR_SHAPE_INVALID, "mf_ckpt_quant_fp8: chunk %d has %lld elements", i, (long long)d.n);
+            return fail(MF_ERR_INVALID_ARGUMENT, "%s: chunk %d names tensor %d of %d", name, i, d.tensor, n_tensors);
+        if (d.n < 0) return fail(MF_ERR_SHAPE_INVALID, "%s: chunk %d has %lld elements", name, i, (long long)d.n);
         if (!is_float_store_dtype(d.src_dtype))
-            return fail(MF_ERR_DTYPE_UNSUPPORTED, "mf_ckpt_quant_fp8: chunk %d source dtype %d unsupported", i, d.src_dtype);
-        if (d.n > 0 && (!d.src || !d.dst)) return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8: chunk %d has a NULL buffer", i);
+            return fail(MF_ERR_DTYPE_UNSUPPORTED, "%s: chunk %d source dtype %d unsupported", name, i, d.src_dtype);
+        if (d.n > 0 && (!d.src || !d.dst)) return fail(MF_ERR_INVALID_ARGUMENT, "%s: chunk %d has a NULL buffer", name, i);
     }
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    MF_CUDA_CHECK(cudaMemsetAsync(d_amax, 0, sizeof(float) * n_tensors, s));
-    static GroupArgs args;  // large; filled and consumed by value at launch on this thread
-    static std::mutex args_mutex;
-    std::lock_guard<std::mutex> lock(args_mutex);
+    return MF_OK;
+}
+
+static int check_fp8_mode(const char* name, int fp8_dtype, int compat) {
+    if (!is_fp8(fp8_dtype)) return fail(MF_ERR_DTYPE_UNSUPPORTED, "%s: dtype %d is not FP8", name, fp8_dtype);
+    if (compat != MF_COMPAT_REFERENCE && compat != MF_COMPAT_OCP)
+        return fail(MF_ERR_INVALID_ARGUMENT, "%s: unknown compat mode %d", name, compat);
+    return MF_OK;
+}
+
+namespace {
+std::mutex g_group_mutex;
+GroupArgs g_group_args;  // ~20 KB; filled under the mutex and copied into the launch
+
+int launch_amax_pass(const mf_chunk_desc* chunks, int32_t n_chunks, float* d_amax, cudaStream_t s) {
+    std::lock_guard<std::mutex> lock(g_group_mutex);
+    GroupArgs& args = g_group_args;
     const int grid_cap = state().sm_count * 8;
     for (int32_t first = 0; first < n_chunks; first += kGroupMaxChunks) {
         const int count = std::min<int32_t>(kGroupMaxChunks, n_chunks - first);
         args.amax = d_amax;
-        args.scale_inv = d_scale_inv;
-        args.fp8_dtype = fp8_dtype;
+        args.scale_inv = nullptr;
+        args.fp8_dtype = 0;
         const int64_t tiles = fill_group(args, chunks, first, count);
         if (tiles == 0) continue;
         const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, grid_cap));
         group_amax_kernel<<<blocks, kThreads, 0, s>>>(args);
-        MF_LAUNCH_CHECK("mf_ckpt_quant_fp8 amax launch");
+        MF_LAUNCH_CHECK("checkpoint amax pass launch");
     }
-    if (comm) {
-        int rc = comm_allreduce_max(comm, d_amax, n_tensors, s);
-        if (rc) return rc;
-    }
+    return MF_OK;
+}
+
+int launch_cast_pass(const mf_chunk_desc* chunks, int32_t n_chunks, const float* d_amax, float* d_scale_inv,
+                     int fp8_dtype, int compat, cudaStream_t s) {
+    std::lock_guard<std::mutex> lock(g_group_mutex);
+    GroupArgs& args = g_group_args;
+    const int grid_cap = state().sm_count * 8;
     for (int32_t first = 0; first < n_chunks; first += kGroupMaxChunks) {
         const int count = std::min<int32_t>(kGroupMaxChunks, n_chunks - first);
-        args.amax = d_amax;
+        args.amax = const_cast<float*>(d_amax);
         args.scale_inv = d_scale_inv;
         args.fp8_dtype = fp8_dtype;
         const int64_t tiles = fill_group(args, chunks, first, count);
@@ -610,7 +621,44 @@ extern "C" int mf_ckpt_quant_fp8(const mf_chunk_desc* chunks, int32_t n_chunks, 
             if (compat) group_cast_kernel<MF_DT_F8E5M2, 1><<<blocks, kThreads, 0, s>>>(args);
             else group_cast_kernel<MF_DT_F8E5M2, 0><<<blocks, kThreads, 0, s>>>(args);
         }
-        MF_LAUNCH_CHECK("mf_ckpt_quant_fp8 cast launch");
+        MF_LAUNCH_CHECK("checkpoint cast pass launch");
     }
     return MF_OK;
+}
+}  // namespace
+
+extern "C" int mf_ckpt_amax_pass(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors, float* d_amax,
+                                 mf_stream stream) {
+    MF_ENTER();
+    int rc = check_chunks("mf_ckpt_amax_pass", chunks, n_chunks, n_tensors, d_amax);
+    if (rc) return rc;
+    return launch_amax_pass(chunks, n_chunks, d_amax, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mf_ckpt_cast_pass(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors, const float* d_amax,
+                                 float* d_scale_inv, int fp8_dtype, int compat, mf_stream stream) {
+    MF_ENTER();
+    int rc = check_chunks("mf_ckpt_cast_pass", chunks, n_chunks, n_tensors, d_amax);
+    if (rc) return rc;
+    rc = check_fp8_mode("mf_ckpt_cast_pass", fp8_dtype, compat);
+    if (rc) return rc;
+    return launch_cast_pass(chunks, n_chunks, d_amax, d_scale_inv, fp8_dtype, compat, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mf_ckpt_quant_fp8(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors, float* d_amax,
+                                 float* d_scale_inv, int fp8_dtype, int compat, mf_comm comm, mf_stream stream) {
+    MF_ENTER();
+    int rc = check_chunks("mf_ckpt_quant_fp8", chunks, n_chunks, n_tensors, d_amax);
+    if (rc) return rc;
+    rc = check_fp8_mode("mf_ckpt_quant_fp8", fp8_dtype, compat);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    MF_CUDA_CHECK(cudaMemsetAsync(d_amax, 0, sizeof(float) * n_tensors, s));
+    rc = launch_amax_pass(chunks, n_chunks, d_amax, s);
+    if (rc) return rc;
+    if (comm) {
+        rc = comm_allreduce_max(comm, d_amax, n_tensors, s);
+        if (rc) return rc;
+    }
+    return launch_cast_pass(chunks, n_chunks, d_amax, d_scale_inv, fp8_dtype, compat, s);
 }

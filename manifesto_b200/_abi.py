@@ -93,6 +93,8 @@ SIGNATURES: dict[str, list] = {
     "mf_comm_init": [ctypes.POINTER(_vp), _i32, _i32, _vp],
     "mf_comm_destroy": [_vp],
     "mf_comm_allreduce_max_f32": [_vp, _vp, _i64, _vp],
+    "mf_ckpt_amax_pass": [ctypes.POINTER(ChunkDesc), _i32, _i32, _vp, _vp],
+    "mf_ckpt_cast_pass": [ctypes.POINTER(ChunkDesc), _i32, _i32, _vp, _vp, _int, _int, _vp],
     "mf_ckpt_quant_fp8": [ctypes.POINTER(ChunkDesc), _i32, _i32, _vp, _vp, _int, _int, _vp, _vp],
 }
 
@@ -124,7 +126,14 @@ def last_error() -> str:
 
 
 def call(name: str, *args) -> None:
-    """Call an mf_* entry point and raise the mapped exception on failure."""
+    """Call an mf_* entry point and raise the mapped exception on failure.
+
+    Only entry points with a declared signature may be called: without
+    argtypes ctypes would pass 64-bit pointers and stream handles as 32-bit
+    ints.
+    """
+    if name not in SIGNATURES:
+        raise KeyError(f"{name} has no declared ctypes signature in manifesto_b200._abi.SIGNATURES")
     rc = getattr(lib(), name)(*args)
     if rc != 0:
         raise_for_status(rc, f"{name}: {last_error()}")

@@ -18,10 +18,11 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// y + alpha * x with the amd64 NaN rule (Go source order: y += alpha*addend).
 template <int FUSED>
 __device__ __forceinline__ float axpy_op(float y, float x, float alpha) {
-    if constexpr (FUSED) return __fmaf_rn(alpha, x, y);
-    else return __fadd_rn(y, __fmul_rn(alpha, x));
+    if constexpr (FUSED) return x86_fma(alpha, x, y);
+    else return x86_add(y, x86_mul(alpha, x));
 }
 
 template <int DT, int FUSED>
@@ -80,10 +81,10 @@ int launch_axpy(void* y, const void* x, int64_t n, float alpha, int fused, cudaS
 
 template <int OP>
 __device__ __forceinline__ float scalar_op(float v, float s) {
-    if constexpr (OP == MF_SCALAR_ADD) return __fadd_rn(v, s);
-    else if constexpr (OP == MF_SCALAR_SUB) return __fsub_rn(v, s);
-    else if constexpr (OP == MF_SCALAR_MUL) return __fmul_rn(v, s);
-    else return __fdiv_rn(v, s);
+    if constexpr (OP == MF_SCALAR_ADD) return x86_add(v, s);
+    else if constexpr (OP == MF_SCALAR_SUB) return x86_sub(v, s);
+    else if constexpr (OP == MF_SCALAR_MUL) return x86_mul(v, s);
+    else return x86_div(v, s);
 }
 
 template <int SRC, int DST, int OP>

@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(kThreads) int4_dequant_vec_kernel(const uint4*
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
 #pragma unroll
-            for (int k = 0; k < 8; ++k) v[8 * j + k] = __fmul_rn(nibble_f32(w[j], k), s);
+            for (int k = 0; k < 8; ++k) v[8 * j + k] = x86_mul(nibble_f32(w[j], k), s);
         }
         if constexpr (ODT == MF_DT_F32) {
             uint4* o = reinterpret_cast<uint4*>(out) + c * 8;
@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(kThreads) int4_dequant_scalar_kernel(const uin
         const int64_t r = e / cols;
         const int64_t col = e - r * cols;
         const float qv = load_as_f32<MF_DT_I4>(q, e);
-        const float v = __fmul_rn(qv, load_scale<SDT>(scales, r * ngroups + col / group));
+        const float v = x86_mul(qv, load_scale<SDT>(scales, r * ngroups + col / group));
         store_code<ODT>(out, e, encode_f32<ODT>(v, 0));
     }
 }

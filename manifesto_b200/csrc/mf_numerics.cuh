@@ -167,6 +167,31 @@ __device__ __forceinline__ uint32_t f16_to_f32bits(uint32_t h) {
     return sign | r;
 }
 
+// ------------------------------------------- amd64 NaN rule for f32 ops
+
+// The GPU returns the canonical NaN 0x7FFFFFFF for any NaN result; the
+// reference's Go code runs on amd64, where SSE propagates a NaN operand
+// (quieted; the first operand as written when both are NaN) and produces
+// the default NaN 0xFFC00000 for invalid operations on non-NaN operands.
+// These wrappers keep the IEEE result and only rewrite NaN results, so
+// they cost one compare on the common path.
+__device__ __forceinline__ float x86_nan2(float a, float b) {
+    if (a != a) return __uint_as_float(__float_as_uint(a) | 0x400000u);
+    if (b != b) return __uint_as_float(__float_as_uint(b) | 0x400000u);
+    return __uint_as_float(0xffc00000u);
+}
+__device__ __forceinline__ float x86_add(float a, float b) { const float r = __fadd_rn(a, b); return r != r ? x86_nan2(a, b) : r; }
+__device__ __forceinline__ float x86_sub(float a, float b) { const float r = __fsub_rn(a, b); return r != r ? x86_nan2(a, b) : r; }
+__device__ __forceinline__ float x86_mul(float a, float b) { const float r = __fmul_rn(a, b); return r != r ? x86_nan2(a, b) : r; }
+__device__ __forceinline__ float x86_div(float a, float b) { const float r = __fdiv_rn(a, b); return r != r ? x86_nan2(a, b) : r; }
+__device__ __forceinline__ float x86_fma(float a, float b, float c) {
+    const float r = __fmaf_rn(a, b, c);
+    if (r == r) return r;
+    if ((a != a) | (b != b)) return x86_nan2(a, b);
+    if (c != c) return __uint_as_float(__float_as_uint(c) | 0x400000u);
+    return __uint_as_float(0xffc00000u);
+}
+
 // ------------------------------------------------- approximate math
 
 // 2^x and 1/x on the SFU (PTX ex2.approx.f32 / rcp.approx.f32, subnormals kept).

@@ -27,6 +27,30 @@ enum {
 static inline float f_from_bits(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
 static inline uint32_t bits_from_f(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
 
+/* float32 arithmetic with the amd64 (SSE) NaN rule, made explicit so the
+ * result does not depend on which operand order a compiler picks: a NaN
+ * operand propagates quieted (the first operand as written in the Go source
+ * when both are NaN); an invalid operation on non-NaN operands (0 * inf,
+ * inf - inf, 0 / 0) yields the x86 default NaN 0xFFC00000.  This is what
+ * the reference's `y += alpha*x` (runtime/axpy.go:116) and
+ * applyScalarBroadcast (runtime/executor_math.go:203-229) produce on amd64. */
+static float nan2(float a, float b) {
+    if (isnan(a)) return f_from_bits(bits_from_f(a) | 0x400000u);
+    if (isnan(b)) return f_from_bits(bits_from_f(b) | 0x400000u);
+    return f_from_bits(0xffc00000u);
+}
+static float x86_add(float a, float b) { float r = a + b; return isnan(r) ? nan2(a, b) : r; }
+static float x86_sub(float a, float b) { float r = a - b; return isnan(r) ? nan2(a, b) : r; }
+static float x86_mul(float a, float b) { float r = a * b; return isnan(r) ? nan2(a, b) : r; }
+static float x86_div(float a, float b) { float r = a / b; return isnan(r) ? nan2(a, b) : r; }
+static float x86_fma(float a, float b, float c) {
+    float r = fmaf(a, b, c);
+    if (!isnan(r)) return r;
+    if (isnan(a) || isnan(b)) return nan2(a, b);
+    if (isnan(c)) return f_from_bits(bits_from_f(c) | 0x400000u);
+    return f_from_bits(0xffc00000u);
+}
+
 /* ---------------------------------------------------------------- FP8 */
 
 /* roundToNearestEven, dtype/fp8.go:263-284 */
@@ -362,7 +386,7 @@ int ref_int4_dequant_grouped(const uint8_t* q, const void* scales, int scale_dty
             float s;
             int rc = decode_one(scale_dtype, scales, r * ngroups + c / group, &s);
             if (rc) return rc;
-            float v = (float)nib * s;
+            float v = x86_mul((float)nib, s);
             rc = encode_one(out_dtype, v, out, e, 0);
             if (rc) return rc;
         }
@@ -383,10 +407,10 @@ int ref_axpy(void* y, const void* x, int64_t begin, int64_t n, float alpha, int 
         decode_one(dtype, x, i, &xv);
         float r;
         if (fused_fma) {
-            r = fmaf(alpha, xv, yv);
+            r = x86_fma(alpha, xv, yv);
         } else {
-            float t = alpha * xv;
-            r = yv + t;
+            float t = x86_mul(alpha, xv);
+            r = x86_add(yv, t);
         }
         encode_one(dtype, r, y, i, 0);
     }
@@ -405,10 +429,10 @@ int ref_scalar_broadcast(const void* src, int src_dtype, void* dst, int dst_dtyp
         if (rc) return rc;
         float r;
         switch (op) {
-        case 0: r = v + scalar; break;
-        case 1: r = v - scalar; break;
-        case 2: r = v * scalar; break;
-        default: r = v / scalar; break;
+        case 0: r = x86_add(v, scalar); break;
+        case 1: r = x86_sub(v, scalar); break;
+        case 2: r = x86_mul(v, scalar); break;
+        default: r = x86_div(v, scalar); break;
         }
         rc = encode_one(dst_dtype, r, dst, i, 0);
         if (rc) return rc;

@@ -26,7 +26,14 @@ def test_library_exports_every_declared_symbol():
     assert len(names) >= 40
     for name in names:
         assert hasattr(L, name), name
-    assert set(_abi.SIGNATURES) | {"mf_last_error"} >= set(names) - {"mf_last_error_copy"} or True
+    # every declared entry point has a ctypes signature (mf_last_error returns a string)
+    assert set(names) - {"mf_last_error"} == set(_abi.SIGNATURES)
+
+
+def test_call_refuses_undeclared_entry_points():
+    from manifesto_b200 import _abi
+    with pytest.raises(KeyError):
+        _abi.call("mf_not_declared")
 
 
 def test_abi_version_and_no_device_paths():

@@ -118,6 +118,20 @@ def test_axpy_matches_oracle(backend, ref, dt, n, fused):
     bits_equal(run_axpy(y, x, 0.75, dt, fused), ref.axpy(y, x, 0.75, dt, fused))
 
 
+@pytest.mark.parametrize("dt", [F32, BF16])
+@pytest.mark.parametrize("fused", [0, 1])
+def test_axpy_special_values(backend, ref, dt, fused):
+    """NaN payloads, infinities, zeros and huge values: the amd64 NaN rule, bit-exact."""
+    specials = np.array([0x7FC01234, 0xFF812345, 0x7F800000, 0xFF800000, 0x00000000, 0x80000000, 0x7F7FFFFF,
+                         0x00000001, 0x3F800000, 0xBF800000], dtype=np.uint32)
+    x = np.repeat(specials, specials.size)
+    y = np.tile(specials, specials.size)
+    if dt == BF16:
+        x, y = (x >> 16).astype(np.uint16), (y >> 16).astype(np.uint16)
+    for alpha in (0.75, 0.0, float("inf"), float("nan")):
+        bits_equal(run_axpy(y, x, alpha, dt, fused), ref.axpy(y, x, alpha, dt, fused))
+
+
 def test_axpy_unfused_differs_from_fma_somewhere(backend, ref):
     """Both rounding modes are real: on random data they disagree on some elements."""
     n = 1 << 16

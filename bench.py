@@ -197,59 +197,79 @@ def kernel_line(name: str, alg_bytes: float, times_ms: list[float], peak: float,
             "elems_per_s": elems / (ms * 1e-3), "reps": len(times_ms)}
 
 
-def bench_kernels(torch, stream_handle: int, peak: float) -> dict:
-    """Configs 1-4 on one GPU, each kernel timed alone with L2 flushed before every launch."""
-    from manifesto_b200 import fusion
-    from manifesto_b200._abi import call
-    from manifesto_b200.dtype import DType
+KERNEL_CONFIGS = ("c1", "c2", "c3", "c4")
 
+
+def bench_kernels(torch, stream_handle: int, peak: float, which=KERNEL_CONFIGS, reps: int = 20) -> dict:
+    """Configs 1-4 on one GPU, each kernel timed alone with L2 flushed before every launch."""
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
     flush = lambda: flush_buf.fill_(1)
     out = {}
-    reps = 20
+    for name in which:
+        out.update({"c1": _kernel_c1, "c2": _kernel_c2, "c3": _kernel_c3, "c4": _kernel_c4}[name](
+            torch, stream_handle, peak, flush, reps))
+        torch.cuda.empty_cache()
+    del flush_buf
+    torch.cuda.empty_cache()
+    return out
 
-    # config 1: FP8 E4M3 -> FP32, 2^26 elements (all 256 codes uniform)
+
+def _warm(f, k: int = 3) -> None:
+    for _ in range(k):
+        f()
+
+
+def _kernel_c1(torch, stream_handle, peak, flush, reps) -> dict:
+    """Config 1: FP8 E4M3 -> FP32, 2^26 elements (bytes uniform over all 256 codes)."""
+    from manifesto_b200._abi import call
     n = 1 << 26
     src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
     dst = torch.empty(n, dtype=torch.float32, device="cuda")
     f = lambda: call("mf_convert", 5, 2, src.data_ptr(), dst.data_ptr(), n, 0, stream_handle)
-    for _ in range(3):
-        f()
-    out["c1_fp8e4m3_to_f32"] = kernel_line("convert_vec_kernel<E4M3,F32>", 5 * n, time_launches(torch, f, reps, flush),
-                                           peak, n)
-    del src, dst
+    _warm(f)
+    return {"c1_fp8e4m3_to_f32": kernel_line("convert_vec_kernel<E4M3,F32>", 5 * n,
+                                             time_launches(torch, f, reps, flush), peak, n)}
 
-    # config 2: Int4 -> BF16 dequant, 4096 x 14336, group 128, BF16 scales ~ |N(0, 0.02)|
+
+def _kernel_c2(torch, stream_handle, peak, flush, reps) -> dict:
+    """Config 2: Int4 -> BF16 dequant, 4096 x 14336, group 128, BF16 scales ~ |N(0, 0.02)|."""
+    from manifesto_b200._abi import call
     rows, cols, group = 4096, 14336, 128
     q = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device="cuda")
     sc = (torch.randn(rows * cols // group, device="cuda").abs() * 0.02).to(torch.bfloat16)
     o = torch.empty(rows * cols, dtype=torch.bfloat16, device="cuda")
     f = lambda: call("mf_int4_dequant_grouped", q.data_ptr(), sc.data_ptr(), 4, o.data_ptr(), 4, rows, cols, group,
                      stream_handle)
-    for _ in range(3):
-        f()
+    _warm(f)
     b = rows * cols // 2 + sc.numel() * 2 + rows * cols * 2
-    out["c2_int4_to_bf16"] = kernel_line("int4_dequant_vec_kernel<BF16,BF16>", b, time_launches(torch, f, reps, flush),
-                                         peak, rows * cols)
-    del q, sc, o
+    return {"c2_int4_to_bf16": kernel_line("int4_dequant_vec_kernel<BF16,BF16>", b,
+                                           time_launches(torch, f, reps, flush), peak, rows * cols)}
 
-    # config 3: axpy f32 and bf16, N = 2^28, alpha = 0.75
+
+def _kernel_c3(torch, stream_handle, peak, flush, reps) -> dict:
+    """Config 3: axpy y = 0.75 x + y, N = 2^28, in FP32 and in BF16 (FP32 arithmetic)."""
+    from manifesto_b200._abi import call
+    out = {}
     n = 1 << 28
     x = torch.randn(n, device="cuda")
     y = torch.randn(n, device="cuda")
     f = lambda: call("mf_axpy", y.data_ptr(), x.data_ptr(), n, 0.75, 2, 0, stream_handle)
-    for _ in range(3):
-        f()
+    _warm(f)
     out["c3a_axpy_f32"] = kernel_line("axpy_vec_kernel<F32>", 12 * n, time_launches(torch, f, reps, flush), peak, n)
     xb, yb = x.to(torch.bfloat16), y.to(torch.bfloat16)
     del x, y
     f = lambda: call("mf_axpy", yb.data_ptr(), xb.data_ptr(), n, 0.75, 4, 0, stream_handle)
-    for _ in range(3):
-        f()
+    _warm(f)
     out["c3b_axpy_bf16"] = kernel_line("axpy_vec_kernel<BF16>", 6 * n, time_launches(torch, f, reps, flush), peak, n)
-    del xb, yb
+    return out
 
-    # config 4: Mul(Silu(Add(Mul(x, gamma), beta)), y) on BF16 [64, 2048, 4096] -> amax -> E4M3
+
+def _kernel_c4(torch, stream_handle, peak, flush, reps) -> dict:
+    """Config 4: Mul(Silu(Add(Mul(x, gamma), beta)), y) on BF16 [64, 2048, 4096] -> amax -> E4M3."""
+    from manifesto_b200 import fusion
+    from manifesto_b200._abi import call
+    from manifesto_b200.dtype import DType
+    out = {}
     hidden = 4096
     n = 64 * 2048 * hidden
     x = torch.empty(n, dtype=torch.bfloat16, device="cuda")
@@ -266,21 +286,18 @@ def bench_kernels(torch, stream_handle: int, peak: float) -> dict:
                          out_dtype=DType.BFLOAT16)
     ptrs = [x.data_ptr(), g.data_ptr(), be.data_ptr(), y.data_ptr()]
     f = lambda: k.run_fp8(ptrs, pre.data_ptr(), qo.data_ptr(), n, am.data_ptr(), si.data_ptr(), stream=stream_handle)
-    for _ in range(3):
-        f()
+    _warm(f)
     out["c4_fused_swiglu_fp8"] = kernel_line("swiglu_bf16_kernel + scaled_cast_vec_kernel", 9 * n,
                                              time_launches(torch, f, max(5, reps // 2), flush), peak, n)
     f1 = lambda: k.run(ptrs, pre.data_ptr(), n, amax=am.data_ptr(), stream=stream_handle)
-    out["c4_pass1_swiglu"] = kernel_line("swiglu_bf16_kernel<amax>", 6 * n, time_launches(torch, f1, reps // 2, flush),
-                                         peak, n)
+    out["c4_pass1_swiglu"] = kernel_line("swiglu_bf16_kernel<amax>", 6 * n,
+                                         time_launches(torch, f1, max(5, reps // 2), flush), peak, n)
     f2 = lambda: call("mf_fp8_scaled_cast", pre.data_ptr(), 4, qo.data_ptr(), 5, am.data_ptr(), si.data_ptr(), n, 0,
                       stream_handle)
     out["c4_pass2_cast"] = kernel_line("scaled_cast_vec_kernel<BF16,E4M3>", 3 * n,
-                                       time_launches(torch, f2, reps // 2, flush), peak, n)
+                                       time_launches(torch, f2, max(5, reps // 2), flush), peak, n)
     out["c4_fused_swiglu_fp8"]["single_pass_lower_bound_bytes"] = 5 * n
     k.close()
-    del x, y, pre, qo, flush_buf
-    torch.cuda.empty_cache()
     return out
 
 
@@ -297,7 +314,15 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
     stream = torch.cuda.current_stream().cuda_stream
     peak, peak_src = hbm_peak()
 
-    specs = checkpoint.llama3_8b_layout()
+    if args.only_kernels:
+        if rank == 0:
+            which = tuple(args.kernels.split(","))
+            print(json.dumps({"kernels": bench_kernels(torch, stream, peak, which, reps=args.steps)}), flush=True)
+        dist.close()
+        return
+
+    full = args.ckpt_layers == 32 and args.ckpt_vocab == 128256
+    specs = checkpoint.llama3_8b_layout(layers=args.ckpt_layers, vocab=args.ckpt_vocab)
     total_params = sum(s.numel for s in specs)
     parts = checkpoint.partition(specs, world, rank)
     local = [rows * s.cols for (first, rows), s in zip(parts, specs)]
@@ -373,7 +398,7 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
     kernels = None
     cpu = None
     if world == 1 and not args.no_kernels:
-        kernels = bench_kernels(torch, stream, peak)
+        kernels = bench_kernels(torch, stream, peak, tuple(args.kernels.split(",")))
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(steps=2, warmup=0)
 
@@ -384,7 +409,8 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
             "metric": METRIC, "value": value, "unit": "elems/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0, 0.02) BF16 weights)",
-            "config": {"workload": "ckpt_fp8_e4m3_llama3_8b",
+            "config": {"workload": "ckpt_fp8_e4m3_llama3_8b" if full else
+                       f"ckpt_fp8_e4m3_reduced_layers{args.ckpt_layers}_vocab{args.ckpt_vocab} (profiling size)",
                        "description": "whole-checkpoint per-tensor amax-scaled FP8 E4M3 quantisation, Llama-3-8B "
                                       "layout (291 BF16 tensors), rows split over ranks, NCCL max all-reduce of amax",
                        "tensors": len(specs), "params": total_params, "src_dtype": "bf16", "dst_dtype": "fp8e4m3",
@@ -515,6 +541,12 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-config kernel lines (N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernels", default=",".join(KERNEL_CONFIGS),
+                    help="comma list of per-config kernel lines to run at N=1 (c1,c2,c3,c4)")
+    ap.add_argument("--only-kernels", action="store_true",
+                    help="run only the per-config kernel lines (profiling); --steps sets the repetitions")
+    ap.add_argument("--ckpt-layers", type=int, default=32, help="decoder layers of the checkpoint (profiling only)")
+    ap.add_argument("--ckpt-vocab", type=int, default=128256, help="vocabulary rows (profiling only)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

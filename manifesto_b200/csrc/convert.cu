@@ -20,7 +20,7 @@ namespace {
 constexpr int kThreads = 256;
 
 template <int SRC, int DST, int COMPAT>
-__global__ void __launch_bounds__(kThreads) convert_vec_kernel(const void* __restrict__ src,
+__global__ void __launch_bounds__(kThreads, 4) convert_vec_kernel(const void* __restrict__ src,
                                                               void* __restrict__ dst, int64_t n) {
     const int64_t nchunks = n / kChunk;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;

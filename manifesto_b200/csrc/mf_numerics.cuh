@@ -17,6 +17,13 @@ namespace mf {
 
 // ------------------------------------------------------------------ FP8
 
+// Small unsigned integer m (< 2^23) times 2^k, exactly, without I2F:
+// (2^23 + m) * 2^k - 2^(23+k) is exact, so one FFMA on the bit pattern
+// 0x4B000000 | m gives m * 2^k.
+__device__ __forceinline__ float small_uint_scaled(uint32_t m, float two_k, float two_23k) {
+    return __fmaf_rn(__uint_as_float(0x4B000000u | m), two_k, -two_23k);
+}
+
 // E4M3 -> f32 bits, dtype/fp8.go:39-70.  Normal codes widen by re-biasing
 // the exponent (+120); subnormal codes are m * 2^-9 (exact in float32);
 // S.1111.111 is NaN and widens to sign | 0x7fc00000.
@@ -24,7 +31,7 @@ __device__ __forceinline__ uint32_t e4m3_to_f32bits(uint32_t code) {
     const uint32_t sign = (code & 0x80u) << 24;
     const uint32_t mag = code & 0x7fu;
     const uint32_t normal = (mag << 20) + (120u << 23);
-    const uint32_t sub = __float_as_uint(static_cast<float>(mag & 7u) * 0.001953125f);
+    const uint32_t sub = __float_as_uint(small_uint_scaled(mag & 7u, 0.001953125f, 16384.0f));
     uint32_t r = (mag >> 3) ? normal : sub;
     r = (mag == 0x7fu) ? 0x7fc00000u : r;
     return sign | r;
@@ -36,7 +43,7 @@ __device__ __forceinline__ uint32_t e5m2_to_f32bits(uint32_t code) {
     const uint32_t sign = (code & 0x80u) << 24;
     const uint32_t mag = code & 0x7fu;
     const uint32_t normal = (mag << 21) + (112u << 23);
-    const uint32_t sub = __float_as_uint(static_cast<float>(mag & 3u) * 1.52587890625e-05f);
+    const uint32_t sub = __float_as_uint(small_uint_scaled(mag & 3u, 1.52587890625e-05f, 128.0f));
     uint32_t r = (mag >> 2) ? normal : sub;
     const uint32_t special = (mag & 3u) ? (0x7fc00000u | ((mag & 3u) << 21)) : 0x7f800000u;
     r = ((mag >> 2) == 31u) ? special : r;
@@ -160,7 +167,7 @@ __device__ __forceinline__ uint32_t f16_to_f32bits(uint32_t h) {
     const uint32_t sign = (h & 0x8000u) << 16;
     const uint32_t mag = h & 0x7fffu;
     const uint32_t normal = (mag << 13) + (112u << 23);
-    const uint32_t sub = __float_as_uint(static_cast<float>(mag) * 5.9604644775390625e-08f);
+    const uint32_t sub = __float_as_uint(small_uint_scaled(mag & 0x3ffu, 5.9604644775390625e-08f, 0.5f));
     uint32_t r = (mag >> 10) ? normal : sub;
     const uint32_t special = (mag & 0x3ffu) ? (0x7fc00000u | ((mag & 0x3ffu) << 13)) : 0x7f800000u;
     r = ((mag >> 10) == 31u) ? special : r;

@@ -86,6 +86,98 @@ __device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi) {
     return r;
 }
 
+// Four float32 -> four FP8 codes (byte k = v[k]) with the hardware
+// round-to-nearest-even .satfinite conversion (OCP rule, largest finite on
+// overflow and Inf).
+template <int DT>
+__device__ __forceinline__ uint32_t cvt4_fp8_satfinite(float v0, float v1, float v2, float v3) {
+    uint16_t lo, hi;
+    if constexpr (DT == MF_DT_F8E4M3) {
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v1), "f"(v0));
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v3), "f"(v2));
+    } else {
+        asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v1), "f"(v0));
+        asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v3), "f"(v2));
+    }
+    return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// NaN lanes (magnitude 0x7f) -> 0x7f without sign, four bytes at a time.
+__device__ __forceinline__ uint32_t fp8x4_canonical_nan(uint32_t w, uint32_t nan_mag4) {
+    const uint32_t nan = __vcmpgeu4(w & 0x7f7f7f7fu, nan_mag4);
+    return (w & ~nan) | (nan & 0x7f7f7f7fu);
+}
+
+// E4M3 encode of 16 values with the reference's rules (dtype/fp8.go:77-136),
+// fast path: the hardware .satfinite conversion agrees with the reference
+// everywhere except (a) |v| >= 248, where the reference saturates to 0x7e
+// (exponent 15 is never produced), (b) NaN, always 0x7f, and (c) the
+// subnormal band 2^-10 <= |v| < 2^-6, where the reference's shift differs.
+// (a) and (b) are fixed on the packed codes with byte-SIMD compares; a chunk
+// with any element in band (c) is re-encoded with the exact integer routine.
+__device__ __forceinline__ void encode16_e4m3_ref(const float (&v)[kChunk], uint32_t (&w)[4]) {
+    uint32_t band = 0;
+#pragma unroll
+    for (int k = 0; k < kChunk; ++k)
+        band |= static_cast<uint32_t>(((__float_as_uint(v[k]) & 0x7fffffffu) - 0x3a800000u) < 0x02000000u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        uint32_t c = cvt4_fp8_satfinite<MF_DT_F8E4M3>(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        // .satfinite yields magnitude 0x7f (S.1111.111) only for NaN inputs
+        const uint32_t m7 = c & 0x7f7f7f7fu;
+        const uint32_t nan = __vcmpeq4(m7, 0x7f7f7f7fu);
+        const uint32_t big = __vcmpgeu4(m7, 0x78787878u);  // |v| >= 248
+        c = (c & ~big) | (big & ((c & 0x80808080u) | 0x7e7e7e7eu));
+        w[k] = (c & ~nan) | (nan & 0x7f7f7f7fu);
+    }
+    if (band) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t c = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) c |= f32bits_to_e4m3_ref(__float_as_uint(v[4 * k + j])) << (8 * j);
+            w[k] = c;
+        }
+    }
+}
+
+// E5M2 encode of 16 values with the reference's rules (dtype/fp8.go:190-249):
+// the hardware result is kept unless the chunk holds a value in the
+// reference's subnormal band 2^-17 <= |v| < 2^-14, a value above 57344
+// (the reference returns Inf there) or a NaN; such chunks take the exact
+// integer routine.
+__device__ __forceinline__ void encode16_e5m2_ref(const float (&v)[kChunk], uint32_t (&w)[4]) {
+    uint32_t slow = 0;
+#pragma unroll
+    for (int k = 0; k < kChunk; ++k) {
+        const uint32_t a = __float_as_uint(v[k]) & 0x7fffffffu;
+        slow |= static_cast<uint32_t>((a - 0x37000000u) < 0x01800000u) | static_cast<uint32_t>(a > 0x47600000u);
+    }
+    if (slow) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t c = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) c |= f32bits_to_e5m2_ref(__float_as_uint(v[4 * k + j])) << (8 * j);
+            w[k] = c;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) w[k] = cvt4_fp8_satfinite<MF_DT_F8E5M2>(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+    }
+}
+
+// OCP .satfinite encode of 16 values with NaN -> 0x7f.  .satfinite never
+// produces Inf, so a code magnitude of 0x7f (E4M3) or >= 0x7d (E5M2) is NaN.
+template <int DT>
+__device__ __forceinline__ void encode16_fp8_ocp(const float (&v)[kChunk], uint32_t (&w)[4]) {
+    constexpr uint32_t kNanMag = (DT == MF_DT_F8E4M3) ? 0x7f7f7f7fu : 0x7d7d7d7du;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        w[k] = fp8x4_canonical_nan(cvt4_fp8_satfinite<DT>(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]),
+                                   kNanMag);
+}
+
 // Encode 16 float32 values to a storage format.
 template <int DT>
 __device__ __forceinline__ void encode16(const float (&v)[kChunk], RawChunk<dtype_bytes(DT)>& r, int compat) {
@@ -98,14 +190,12 @@ __device__ __forceinline__ void encode16(const float (&v)[kChunk], RawChunk<dtyp
     } else if constexpr (DT == MF_DT_F16) {
 #pragma unroll
         for (int k = 0; k < kChunk / 2; ++k) r.w[k] = f32x2_to_f16x2(v[2 * k], v[2 * k + 1]);
-    } else if constexpr (DT == MF_DT_F8E4M3 || DT == MF_DT_F8E5M2) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            uint32_t w = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) w |= encode_f32<DT>(v[4 * k + j], compat) << (8 * j);
-            r.w[k] = w;
-        }
+    } else if constexpr (DT == MF_DT_F8E4M3) {
+        if (compat) encode16_fp8_ocp<DT>(v, r.w);
+        else encode16_e4m3_ref(v, r.w);
+    } else if constexpr (DT == MF_DT_F8E5M2) {
+        if (compat) encode16_fp8_ocp<DT>(v, r.w);
+        else encode16_e5m2_ref(v, r.w);
     }
 }
 

@@ -25,6 +25,7 @@
 // makes the scales global.
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "mf_internal.h"
 #include "mf_runtime.h"
@@ -245,8 +246,6 @@ __global__ void __launch_bounds__(kThreads) scaled_cast_scalar_kernel(const void
         store_code<FP8>(dst, i, encode_fp8<FP8>(__fmul_rn(load_as_f32<SRC>(src, i), scale), compat));
 }
 
-bool is_vec_src(int dt) { return dt == MF_DT_F32 || dt == MF_DT_F16 || dt == MF_DT_BF16 || dt == MF_DT_F8E4M3 || dt == MF_DT_F8E5M2; }
-
 template <int SRC>
 void amax_dispatch(const void* src, int64_t n, float* d_amax, cudaStream_t s) {
     if (aligned16(src)) {
@@ -284,16 +283,23 @@ void cast_dispatch_fp8(int fp8_dtype, const void* src, void* dst, int64_t n, con
 // ----------------------------------------------------- grouped (ckpt)
 
 constexpr int kGroupMaxChunks = 512;
-constexpr int kTileChunks = 4;                            // 16-element chunks per thread per tile
-constexpr int64_t kTileElems = int64_t(kThreads) * kTileChunks * kChunk;  // 16384
+
+// Per tile every thread owns 128 bytes of source: 4 chunks of 16 BF16/F16
+// elements or 2 chunks of 16 float32.  One launch covers chunks of one
+// source dtype, so each kernel body holds a single decode path.
+template <int SRC>
+struct Tile {
+    static constexpr int kChunks = 128 / (kChunk * dtype_bytes(SRC));
+    static constexpr int64_t kElems = int64_t(kThreads) * kChunks * kChunk;
+};
 
 struct ChunkRec {
     const void* src;
     void* dst;
     int64_t n;
-    int64_t tile_begin;  // first global tile of this chunk
+    int64_t tile_begin;  // first tile of this chunk within the launch
     int32_t tensor;
-    int32_t flags;       // bit 0: 16-byte aligned src and dst; bits 8..15: src dtype
+    int32_t aligned;     // src and dst 16-byte aligned
 };
 
 struct GroupArgs {
@@ -315,32 +321,34 @@ __device__ __forceinline__ int find_chunk(const GroupArgs& a, int64_t t) {
     return lo;
 }
 
-// Running max of one tile of one chunk, by the chunk's source dtype.
+// max|v| over one tile of one chunk (NaN ignored).
 template <int SRC>
 __device__ __forceinline__ float tile_amax(const ChunkRec& ch, int64_t tile) {
-    const int64_t c0 = tile * (kTileElems / kChunk);
+    using T = Tile<SRC>;
+    const int64_t c0 = tile * (T::kElems / kChunk);
     const int64_t full = ch.n / kChunk;
-    uint32_t key = 0;
     float m = 0.0f;
-    if (ch.flags & 1) {
-        RawChunk<dtype_bytes(SRC)> r[kTileChunks];
+    if (ch.aligned) {
+        RawChunk<dtype_bytes(SRC)> r[T::kChunks];
 #pragma unroll
-        for (int k = 0; k < kTileChunks; ++k) {
+        for (int k = 0; k < T::kChunks; ++k) {
             const int64_t c = c0 + k * kThreads + threadIdx.x;
             if (c < full) load_raw<dtype_bytes(SRC)>(ch.src, c, r[k]);
         }
+        uint32_t key = 0;
 #pragma unroll
-        for (int k = 0; k < kTileChunks; ++k) {
+        for (int k = 0; k < T::kChunks; ++k) {
             const int64_t c = c0 + k * kThreads + threadIdx.x;
             if (c < full) key = MagKey<SRC>::fold(r[k], key);
         }
         m = MagKey<SRC>::to_f32(key);
         // ragged end of the chunk: the last n mod 16 elements
-        const int64_t last_tile = (ch.n - 1) / kTileElems;
-        if (tile == last_tile && threadIdx.x < (ch.n % kChunk)) m = fmaxf(m, abs_or_zero<SRC>(ch.src, full * kChunk + threadIdx.x));
+        const int64_t last_tile = (ch.n - 1) / T::kElems;
+        if (tile == last_tile && threadIdx.x < (ch.n % kChunk))
+            m = fmaxf(m, abs_or_zero<SRC>(ch.src, full * kChunk + threadIdx.x));
     } else {
-        const int64_t e0 = tile * kTileElems;
-        for (int64_t i = e0 + threadIdx.x; i < e0 + kTileElems && i < ch.n; i += kThreads)
+        const int64_t e0 = tile * T::kElems;
+        for (int64_t i = e0 + threadIdx.x; i < e0 + T::kElems && i < ch.n; i += kThreads)
             m = fmaxf(m, abs_or_zero<SRC>(ch.src, i));
     }
     return m;
@@ -348,17 +356,18 @@ __device__ __forceinline__ float tile_amax(const ChunkRec& ch, int64_t tile) {
 
 template <int SRC, int FP8, int COMPAT>
 __device__ __forceinline__ void tile_cast(const ChunkRec& ch, int64_t tile, float scale) {
-    const int64_t c0 = tile * (kTileElems / kChunk);
+    using T = Tile<SRC>;
+    const int64_t c0 = tile * (T::kElems / kChunk);
     const int64_t full = ch.n / kChunk;
-    if (ch.flags & 1) {
-        RawChunk<dtype_bytes(SRC)> r[kTileChunks];
+    if (ch.aligned) {
+        RawChunk<dtype_bytes(SRC)> r[T::kChunks];
 #pragma unroll
-        for (int k = 0; k < kTileChunks; ++k) {
+        for (int k = 0; k < T::kChunks; ++k) {
             const int64_t c = c0 + k * kThreads + threadIdx.x;
             if (c < full) load_raw<dtype_bytes(SRC)>(ch.src, c, r[k]);
         }
 #pragma unroll
-        for (int k = 0; k < kTileChunks; ++k) {
+        for (int k = 0; k < T::kChunks; ++k) {
             const int64_t c = c0 + k * kThreads + threadIdx.x;
             if (c < full) {
                 float v[kChunk];
@@ -370,19 +379,17 @@ __device__ __forceinline__ void tile_cast(const ChunkRec& ch, int64_t tile, floa
                 store_raw<1>(ch.dst, c, o);
             }
         }
-        const int64_t last_tile = (ch.n - 1) / kTileElems;
+        const int64_t last_tile = (ch.n - 1) / T::kElems;
         if (tile == last_tile && threadIdx.x < (ch.n % kChunk)) {
             const int64_t i = full * kChunk + threadIdx.x;
             store_code<FP8>(ch.dst, i, encode_fp8<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), scale), COMPAT));
         }
     } else {
-        const int64_t e0 = tile * kTileElems;
-        for (int64_t i = e0 + threadIdx.x; i < e0 + kTileElems && i < ch.n; i += kThreads)
+        const int64_t e0 = tile * T::kElems;
+        for (int64_t i = e0 + threadIdx.x; i < e0 + T::kElems && i < ch.n; i += kThreads)
             store_code<FP8>(ch.dst, i, encode_fp8<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), scale), COMPAT));
     }
 }
-
-__device__ __forceinline__ int chunk_dtype(const ChunkRec& ch) { return (ch.flags >> 8) & 0xff; }
 
 // This CTA's contiguous tile range [t0, t1).
 __device__ __forceinline__ void tile_range(int64_t total, int64_t& t0, int64_t& t1) {
@@ -392,7 +399,8 @@ __device__ __forceinline__ void tile_range(int64_t total, int64_t& t0, int64_t& 
     t1 = t0 + per + (b < extra ? 1 : 0);
 }
 
-__global__ void __launch_bounds__(kThreads) group_amax_kernel(const __grid_constant__ GroupArgs a) {
+template <int SRC>
+__global__ void __launch_bounds__(kThreads, 4) group_amax_kernel(const __grid_constant__ GroupArgs a) {
     int64_t t0, t1;
     tile_range(a.total_tiles, t0, t1);
     if (t0 >= t1) return;
@@ -406,19 +414,14 @@ __global__ void __launch_bounds__(kThreads) group_amax_kernel(const __grid_const
             ++k;
         }
         const ChunkRec& ch = a.chunk[k];
-        const int64_t tile = t - ch.tile_begin;
-        switch (chunk_dtype(ch)) {
-        case MF_DT_BF16: m = fmaxf(m, tile_amax<MF_DT_BF16>(ch, tile)); break;
-        case MF_DT_F16: m = fmaxf(m, tile_amax<MF_DT_F16>(ch, tile)); break;
-        default: m = fmaxf(m, tile_amax<MF_DT_F32>(ch, tile)); break;
-        }
+        m = fmaxf(m, tile_amax<SRC>(ch, t - ch.tile_begin));
     }
     const float bm = block_max(m);
     if (threadIdx.x == 0) atomic_max_nonneg(a.amax + a.chunk[k].tensor, bm);
 }
 
-template <int FP8, int COMPAT>
-__global__ void __launch_bounds__(kThreads) group_cast_kernel(const __grid_constant__ GroupArgs a) {
+template <int SRC, int FP8, int COMPAT>
+__global__ void __launch_bounds__(kThreads, 4) group_cast_kernel(const __grid_constant__ GroupArgs a) {
     int64_t t0, t1;
     tile_range(a.total_tiles, t0, t1);
     if (t0 >= t1) return;
@@ -433,29 +436,26 @@ __global__ void __launch_bounds__(kThreads) group_cast_kernel(const __grid_const
         const int64_t tile = t - ch.tile_begin;
         if (tile == 0 && threadIdx.x == 0 && a.scale_inv)
             a.scale_inv[ch.tensor] = scale_inv_from_amax(a.amax[ch.tensor], FP8);
-        switch (chunk_dtype(ch)) {
-        case MF_DT_BF16: tile_cast<MF_DT_BF16, FP8, COMPAT>(ch, tile, scale); break;
-        case MF_DT_F16: tile_cast<MF_DT_F16, FP8, COMPAT>(ch, tile, scale); break;
-        default: tile_cast<MF_DT_F32, FP8, COMPAT>(ch, tile, scale); break;
-        }
+        tile_cast<SRC, FP8, COMPAT>(ch, tile, scale);
     }
 }
 
-// Fill `a` from chunks[first, first+count); returns the number of tiles.
-int64_t fill_group(GroupArgs& a, const mf_chunk_desc* chunks, int first, int count) {
+// Fill `a` with the chunks listed in idx[first, first+count); returns the
+// number of tiles of `tile_elems` elements.
+int64_t fill_group(GroupArgs& a, const mf_chunk_desc* chunks, const int32_t* idx, int first, int count,
+                   int64_t tile_elems) {
     int64_t tiles = 0;
     int used = 0;
     for (int i = 0; i < count; ++i) {
-        const mf_chunk_desc& d = chunks[first + i];
-        if (d.n <= 0) continue;
+        const mf_chunk_desc& d = chunks[idx[first + i]];
         ChunkRec& r = a.chunk[used++];
         r.src = d.src;
         r.dst = d.dst;
         r.n = d.n;
         r.tile_begin = tiles;
         r.tensor = d.tensor;
-        r.flags = ((aligned16(d.src) && aligned16(d.dst)) ? 1 : 0) | (d.src_dtype << 8);
-        tiles += (d.n + kTileElems - 1) / kTileElems;
+        r.aligned = (aligned16(d.src) && aligned16(d.dst)) ? 1 : 0;
+        tiles += (d.n + tile_elems - 1) / tile_elems;
     }
     a.n_chunks = used;
     a.total_tiles = tiles;
@@ -583,47 +583,78 @@ namespace {
 std::mutex g_group_mutex;
 GroupArgs g_group_args;  // ~20 KB; filled under the mutex and copied into the launch
 
-int launch_amax_pass(const mf_chunk_desc* chunks, int32_t n_chunks, float* d_amax, cudaStream_t s) {
-    std::lock_guard<std::mutex> lock(g_group_mutex);
+// Chunk indices with n > 0, grouped by source dtype (BF16, F16, F32), each
+// group in table order.
+void group_by_dtype(const mf_chunk_desc* chunks, int32_t n_chunks, std::vector<int32_t> (&by)[3]) {
+    for (int32_t i = 0; i < n_chunks; ++i) {
+        if (chunks[i].n <= 0) continue;
+        const int d = chunks[i].src_dtype;
+        by[d == MF_DT_BF16 ? 0 : d == MF_DT_F16 ? 1 : 2].push_back(i);
+    }
+}
+
+template <int SRC>
+int amax_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, float* d_amax, cudaStream_t s) {
     GroupArgs& args = g_group_args;
     const int grid_cap = state().sm_count * 8;
-    for (int32_t first = 0; first < n_chunks; first += kGroupMaxChunks) {
-        const int count = std::min<int32_t>(kGroupMaxChunks, n_chunks - first);
+    for (int first = 0; first < static_cast<int>(idx.size()); first += kGroupMaxChunks) {
+        const int count = std::min<int>(kGroupMaxChunks, static_cast<int>(idx.size()) - first);
         args.amax = d_amax;
         args.scale_inv = nullptr;
         args.fp8_dtype = 0;
-        const int64_t tiles = fill_group(args, chunks, first, count);
+        const int64_t tiles = fill_group(args, chunks, idx.data(), first, count, Tile<SRC>::kElems);
         if (tiles == 0) continue;
         const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, grid_cap));
-        group_amax_kernel<<<blocks, kThreads, 0, s>>>(args);
+        group_amax_kernel<SRC><<<blocks, kThreads, 0, s>>>(args);
         MF_LAUNCH_CHECK("checkpoint amax pass launch");
     }
     return MF_OK;
 }
 
-int launch_cast_pass(const mf_chunk_desc* chunks, int32_t n_chunks, const float* d_amax, float* d_scale_inv,
-                     int fp8_dtype, int compat, cudaStream_t s) {
-    std::lock_guard<std::mutex> lock(g_group_mutex);
+template <int SRC>
+int cast_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, const float* d_amax,
+                  float* d_scale_inv, int fp8_dtype, int compat, cudaStream_t s) {
     GroupArgs& args = g_group_args;
     const int grid_cap = state().sm_count * 8;
-    for (int32_t first = 0; first < n_chunks; first += kGroupMaxChunks) {
-        const int count = std::min<int32_t>(kGroupMaxChunks, n_chunks - first);
+    for (int first = 0; first < static_cast<int>(idx.size()); first += kGroupMaxChunks) {
+        const int count = std::min<int>(kGroupMaxChunks, static_cast<int>(idx.size()) - first);
         args.amax = const_cast<float*>(d_amax);
         args.scale_inv = d_scale_inv;
         args.fp8_dtype = fp8_dtype;
-        const int64_t tiles = fill_group(args, chunks, first, count);
+        const int64_t tiles = fill_group(args, chunks, idx.data(), first, count, Tile<SRC>::kElems);
         if (tiles == 0) continue;
         const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, grid_cap));
         if (fp8_dtype == MF_DT_F8E4M3) {
-            if (compat) group_cast_kernel<MF_DT_F8E4M3, 1><<<blocks, kThreads, 0, s>>>(args);
-            else group_cast_kernel<MF_DT_F8E4M3, 0><<<blocks, kThreads, 0, s>>>(args);
+            if (compat) group_cast_kernel<SRC, MF_DT_F8E4M3, 1><<<blocks, kThreads, 0, s>>>(args);
+            else group_cast_kernel<SRC, MF_DT_F8E4M3, 0><<<blocks, kThreads, 0, s>>>(args);
         } else {
-            if (compat) group_cast_kernel<MF_DT_F8E5M2, 1><<<blocks, kThreads, 0, s>>>(args);
-            else group_cast_kernel<MF_DT_F8E5M2, 0><<<blocks, kThreads, 0, s>>>(args);
+            if (compat) group_cast_kernel<SRC, MF_DT_F8E5M2, 1><<<blocks, kThreads, 0, s>>>(args);
+            else group_cast_kernel<SRC, MF_DT_F8E5M2, 0><<<blocks, kThreads, 0, s>>>(args);
         }
         MF_LAUNCH_CHECK("checkpoint cast pass launch");
     }
     return MF_OK;
+}
+
+int launch_amax_pass(const mf_chunk_desc* chunks, int32_t n_chunks, float* d_amax, cudaStream_t s) {
+    std::lock_guard<std::mutex> lock(g_group_mutex);
+    std::vector<int32_t> by[3];
+    group_by_dtype(chunks, n_chunks, by);
+    int rc = amax_launches<MF_DT_BF16>(chunks, by[0], d_amax, s);
+    if (!rc) rc = amax_launches<MF_DT_F16>(chunks, by[1], d_amax, s);
+    if (!rc) rc = amax_launches<MF_DT_F32>(chunks, by[2], d_amax, s);
+    return rc;
+}
+
+int launch_cast_pass(const mf_chunk_desc* chunks, int32_t n_chunks, const float* d_amax, float* d_scale_inv,
+                     int fp8_dtype, int compat, cudaStream_t s) {
+    std::lock_guard<std::mutex> lock(g_group_mutex);
+    std::vector<int32_t> by[3];
+    group_by_dtype(chunks, n_chunks, by);
+    int rc = cast_launches<MF_DT_BF16>(chunks, by[0], d_amax, d_scale_inv, fp8_dtype, compat, s);
+    if (!rc) rc = cast_launches<MF_DT_F16>(chunks, by[1], d_amax, d_scale_inv, fp8_dtype, compat, s);
+    if (!rc) rc = cast_launches<MF_DT_F32>(chunks, by[2], d_amax, d_scale_inv, fp8_dtype, compat, s);
+    return rc;
 }
 }  // namespace
 

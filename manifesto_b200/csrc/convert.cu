@@ -5,55 +5,20 @@
 // BytesToFloat8E5M2 (dtype/convert/convert.go:85-228): decode the source
 // element to float32, then encode it with the destination's scalar encoder.
 //
-// Layout: flat arrays of n elements.  The fast path handles the floating
-// formats {F32, F16, BF16, E4M3, E5M2} in 16-element chunks with 128-bit
-// loads and stores (grid-stride, grid capped at a few waves of resident
-// CTAs); the tail (n mod 16), unaligned pointers and the integer / F64 /
-// Int4 sources use a scalar grid-stride kernel with the same codecs.
+// Layout: flat arrays of n elements.  The floating formats {F32, F16, BF16,
+// E4M3, E5M2} with 16-byte aligned buffers run on the bulk-copy streaming
+// engine (mf_stream.cuh): the source is staged through shared memory by
+// cp.async.bulk, decoded and re-encoded 16 elements at a time, and written
+// with 128-bit stores.  Unaligned buffers and the integer / F64 / Int4
+// sources use a scalar grid-stride kernel with the same codecs.
 // Roofline: HBM, src_bytes + dst_bytes per element.
 #include "mf_runtime.h"
-#include "mf_vec.cuh"
+#include "mf_stream.cuh"
 
 namespace mf {
 namespace {
 
 constexpr int kThreads = 256;
-
-template <int SRC, int DST, int COMPAT>
-__global__ void __launch_bounds__(kThreads, 4) convert_vec_kernel(const void* __restrict__ src,
-                                                              void* __restrict__ dst, int64_t n) {
-    const int64_t nchunks = n / kChunk;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    // Two chunks per iteration so each thread keeps two independent loads in flight.
-    for (; c + stride < nchunks; c += 2 * stride) {
-        RawChunk<dtype_bytes(SRC)> r0, r1;
-        load_raw<dtype_bytes(SRC)>(src, c, r0);
-        load_raw<dtype_bytes(SRC)>(src, c + stride, r1);
-        float v[kChunk];
-        RawChunk<dtype_bytes(DST)> o;
-        decode16<SRC>(r0, v);
-        encode16<DST>(v, o, COMPAT);
-        store_raw<dtype_bytes(DST)>(dst, c, o);
-        decode16<SRC>(r1, v);
-        encode16<DST>(v, o, COMPAT);
-        store_raw<dtype_bytes(DST)>(dst, c + stride, o);
-    }
-    if (c < nchunks) {
-        RawChunk<dtype_bytes(SRC)> r0;
-        load_raw<dtype_bytes(SRC)>(src, c, r0);
-        float v[kChunk];
-        RawChunk<dtype_bytes(DST)> o;
-        decode16<SRC>(r0, v);
-        encode16<DST>(v, o, COMPAT);
-        store_raw<dtype_bytes(DST)>(dst, c, o);
-    }
-    // Tail: the last n mod 16 elements, one per thread of the first block.
-    if (blockIdx.x == 0) {
-        const int64_t i = nchunks * kChunk + threadIdx.x;
-        if (i < n) store_code<DST>(dst, i, encode_f32<DST>(load_as_f32<SRC>(src, i), COMPAT));
-    }
-}
 
 __device__ __forceinline__ float decode_any(int dt, const void* p, int64_t i) {
     switch (dt) {
@@ -90,22 +55,21 @@ bool is_vector_format(int dt) {
 }
 
 template <int SRC, int DST>
-void launch_vec(const void* src, void* dst, int64_t n, int compat, cudaStream_t s) {
-    const int64_t blocks = stream_grid(n / kChunk / 2 + 1, kThreads, 8);
-    if (compat)
-        convert_vec_kernel<SRC, DST, 1><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n);
-    else
-        convert_vec_kernel<SRC, DST, 0><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n);
+cudaError_t launch_vec(const void* src, void* dst, int64_t n, int compat, cudaStream_t s) {
+    StreamArgs<1> a{};
+    single_chunk(a, src, dst, n, true);
+    if (compat) return launch_stream<ConvertOp<SRC, DST, 1>, 1>(a, state().sm_count, s);
+    return launch_stream<ConvertOp<SRC, DST, 0>, 1>(a, state().sm_count, s);
 }
 
 template <int SRC>
-void dispatch_dst(int dst_dt, const void* src, void* dst, int64_t n, int compat, cudaStream_t s) {
+cudaError_t dispatch_dst(int dst_dt, const void* src, void* dst, int64_t n, int compat, cudaStream_t s) {
     switch (dst_dt) {
-    case MF_DT_F32: launch_vec<SRC, MF_DT_F32>(src, dst, n, compat, s); break;
-    case MF_DT_F16: launch_vec<SRC, MF_DT_F16>(src, dst, n, compat, s); break;
-    case MF_DT_BF16: launch_vec<SRC, MF_DT_BF16>(src, dst, n, compat, s); break;
-    case MF_DT_F8E4M3: launch_vec<SRC, MF_DT_F8E4M3>(src, dst, n, compat, s); break;
-    default: launch_vec<SRC, MF_DT_F8E5M2>(src, dst, n, compat, s); break;
+    case MF_DT_F32: return launch_vec<SRC, MF_DT_F32>(src, dst, n, compat, s);
+    case MF_DT_F16: return launch_vec<SRC, MF_DT_F16>(src, dst, n, compat, s);
+    case MF_DT_BF16: return launch_vec<SRC, MF_DT_BF16>(src, dst, n, compat, s);
+    case MF_DT_F8E4M3: return launch_vec<SRC, MF_DT_F8E4M3>(src, dst, n, compat, s);
+    default: return launch_vec<SRC, MF_DT_F8E5M2>(src, dst, n, compat, s);
     }
 }
 
@@ -134,13 +98,15 @@ extern "C" int mf_convert(int src_dtype, int dst_dtype, const void* src, void* d
     if (!src || !dst) return fail(MF_ERR_INVALID_ARGUMENT, "mf_convert: NULL buffer");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (is_vector_format(src_dtype) && aligned16(src) && aligned16(dst)) {
+        cudaError_t err;
         switch (src_dtype) {
-        case MF_DT_F32: dispatch_dst<MF_DT_F32>(dst_dtype, src, dst, n, compat, s); break;
-        case MF_DT_F16: dispatch_dst<MF_DT_F16>(dst_dtype, src, dst, n, compat, s); break;
-        case MF_DT_BF16: dispatch_dst<MF_DT_BF16>(dst_dtype, src, dst, n, compat, s); break;
-        case MF_DT_F8E4M3: dispatch_dst<MF_DT_F8E4M3>(dst_dtype, src, dst, n, compat, s); break;
-        default: dispatch_dst<MF_DT_F8E5M2>(dst_dtype, src, dst, n, compat, s); break;
+        case MF_DT_F32: err = dispatch_dst<MF_DT_F32>(dst_dtype, src, dst, n, compat, s); break;
+        case MF_DT_F16: err = dispatch_dst<MF_DT_F16>(dst_dtype, src, dst, n, compat, s); break;
+        case MF_DT_BF16: err = dispatch_dst<MF_DT_BF16>(dst_dtype, src, dst, n, compat, s); break;
+        case MF_DT_F8E4M3: err = dispatch_dst<MF_DT_F8E4M3>(dst_dtype, src, dst, n, compat, s); break;
+        default: err = dispatch_dst<MF_DT_F8E5M2>(dst_dtype, src, dst, n, compat, s); break;
         }
+        if (err != cudaSuccess) return cuda_fail(err, "mf_convert launch");
     } else {
         switch (dst_dtype) {
         case MF_DT_F32: launch_scalar<MF_DT_F32>(src_dtype, src, dst, n, compat, s); break;

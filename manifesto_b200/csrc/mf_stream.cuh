@@ -1,0 +1,342 @@
+// mf_stream.cuh -- the bulk-copy streaming engine shared by the conversion
+// and FP8 cast kernels.
+//
+// Every element-wise map in this library reads its source once and writes
+// its destination once, so its speed is set by how many source bytes are in
+// flight per SM.  Issuing plain loads from every thread ties that to the
+// register budget and serialises "load, then compute" inside each thread.
+// Here one thread per CTA streams the source through a ring of shared-memory
+// stages with the Blackwell bulk-copy engine (cp.async.bulk, 1-D, completion
+// counted on an mbarrier), kStages tiles ahead of the consumers; all 256
+// threads decode the staged tile from shared memory, compute, and write the
+// result with 128-bit streaming stores.  The copy engine keeps up to
+// kStages x 3 CTAs x tile bytes of reads in flight per SM without any
+// register cost, and the loads of later tiles overlap the compute of the
+// current one.
+//
+// Work is a table of chunks (ChunkRec: src, dst, n, tensor); chunks are cut
+// into tiles of kTileElems elements and every CTA walks a contiguous range
+// of tiles (few chunk changes per CTA).  A chunk whose src or dst is not
+// 16-byte aligned is processed with plain loads (the producer arrives on the
+// stage barrier without a copy).  Ragged chunk ends (n not a multiple of 16)
+// are finished with per-element loads.
+//
+// Waits on an mbarrier are bounded: after kMbarSpinLimit polls the CTA
+// records MF_DEVICE_TIMEOUT in the sticky status word, waits (again bounded)
+// for the copies it issued, and returns.
+#pragma once
+
+#include "mf_vec.cuh"
+
+namespace mf {
+
+constexpr int kStreamThreads = 256;
+constexpr int64_t kTileElems = 8192;            // elements per tile
+constexpr int kStreamSmemBudget = 64 * 1024;    // staging bytes per CTA (3 CTAs per SM)
+constexpr uint32_t kMbarSpinLimit = 1u << 24;   // polls of try_wait before giving up
+constexpr int kDeviceTimeout = 0x7100;          // sticky status code of a timed-out wait
+
+struct ChunkRec {
+    const void* src;
+    void* dst;
+    int64_t n;
+    int64_t tile_begin;  // first tile of this chunk within the launch
+    int32_t tensor;
+    int32_t aligned;     // src and dst 16-byte aligned
+};
+
+template <int MaxChunks>
+struct StreamArgs {
+    const float* amax;   // per-tensor amax (cast ops)
+    float* scale_inv;    // per-tensor 1/scale output (cast ops), may be NULL
+    int* status;         // sticky status word
+    int64_t total_tiles;
+    int32_t n_chunks;
+    int32_t pad;
+    ChunkRec chunk[MaxChunks];
+};
+
+// ------------------------------------------------------------ PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    // make the initialised barriers visible to the async (bulk-copy) proxy
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kMbarSpinLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory; completion is counted in
+// bytes on `bar`.  dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+template <int Bytes>
+__device__ __forceinline__ void load_raw_smem(const uint8_t* tile, int c, RawChunk<Bytes>& r) {
+    const uint4* p = reinterpret_cast<const uint4*>(tile) + c * Bytes;
+#pragma unroll
+    for (int k = 0; k < Bytes; ++k) {
+        const uint4 v = p[k];
+        r.w[4 * k + 0] = v.x;
+        r.w[4 * k + 1] = v.y;
+        r.w[4 * k + 2] = v.z;
+        r.w[4 * k + 3] = v.w;
+    }
+}
+
+// ----------------------------------------------------------------- ops
+
+// Plain conversion src -> dst (mf_convert).
+template <int SRC, int DST, int COMPAT>
+struct ConvertOp {
+    static constexpr int kIn = dtype_bytes(SRC);
+    struct State {};
+    template <class A>
+    __device__ static State setup(const A&, const ChunkRec&) { return {}; }
+    template <class A>
+    __device__ static void first_tile(const A&, const ChunkRec&) {}
+    __device__ static void chunk16(const RawChunk<kIn>& r, const ChunkRec& ch, int64_t c, const State&) {
+        float v[kChunk];
+        decode16<SRC>(r, v);
+        RawChunk<dtype_bytes(DST)> o;
+        encode16<DST>(v, o, COMPAT);
+        store_raw<dtype_bytes(DST)>(ch.dst, c, o);
+    }
+    __device__ static void element(const ChunkRec& ch, int64_t i, const State&) {
+        store_code<DST>(ch.dst, i, encode_f32<DST>(load_as_f32<SRC>(ch.src, i), COMPAT));
+    }
+};
+
+__host__ __device__ inline float fp8_max_of(int fp8_dtype) { return fp8_dtype == MF_DT_F8E5M2 ? 57344.0f : 448.0f; }
+
+__device__ __forceinline__ float scale_from_amax(float amax, int fp8_dtype) {
+    const bool ok = (amax > 0.0f) && (amax < __int_as_float(0x7f800000));
+    return ok ? __fdiv_rn(fp8_max_of(fp8_dtype), amax) : 1.0f;
+}
+__device__ __forceinline__ float scale_inv_from_amax(float amax, int fp8_dtype) {
+    const bool ok = (amax > 0.0f) && (amax < __int_as_float(0x7f800000));
+    return ok ? __fdiv_rn(amax, fp8_max_of(fp8_dtype)) : 1.0f;
+}
+
+// Per-tensor amax-scaled FP8 cast: q = encode(v * (fp8_max / amax[tensor])).
+template <int SRC, int FP8, int COMPAT>
+struct CastOp {
+    static constexpr int kIn = dtype_bytes(SRC);
+    struct State {
+        float scale;
+    };
+    template <class A>
+    __device__ static State setup(const A& a, const ChunkRec& ch) {
+        return {scale_from_amax(a.amax[ch.tensor], FP8)};
+    }
+    template <class A>
+    __device__ static void first_tile(const A& a, const ChunkRec& ch) {
+        if (a.scale_inv) a.scale_inv[ch.tensor] = scale_inv_from_amax(a.amax[ch.tensor], FP8);
+    }
+    __device__ static void chunk16(const RawChunk<kIn>& r, const ChunkRec& ch, int64_t c, const State& st) {
+        float v[kChunk];
+        decode16<SRC>(r, v);
+#pragma unroll
+        for (int k = 0; k < kChunk; k += 2) {
+            const float2 p = __fmul2_rn(make_float2(v[k], v[k + 1]), make_float2(st.scale, st.scale));
+            v[k] = p.x;
+            v[k + 1] = p.y;
+        }
+        RawChunk<1> o;
+        encode16<FP8>(v, o, COMPAT);
+        store_raw<1>(ch.dst, c, o);
+    }
+    __device__ static void element(const ChunkRec& ch, int64_t i, const State& st) {
+        store_code<FP8>(ch.dst, i, encode_f32<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), st.scale), COMPAT));
+    }
+};
+
+// ------------------------------------------------------------- the engine
+
+template <class Op>
+struct StreamGeometry {
+    static constexpr int kTileBytes = static_cast<int>(kTileElems) * Op::kIn;
+    static constexpr int kStages = (kStreamSmemBudget / kTileBytes) < 8 ? (kStreamSmemBudget / kTileBytes) : 8;
+    static constexpr int kSmemBytes = kStages * kTileBytes + kStages * 8;
+    static_assert(kStages >= 2, "tile too large for the staging budget");
+};
+
+template <int MaxChunks>
+__device__ __forceinline__ int stream_find_chunk(const StreamArgs<MaxChunks>& a, int64_t t, int from) {
+    int k = from;
+    while (k + 1 < a.n_chunks && a.chunk[k + 1].tile_begin <= t) ++k;
+    return k;
+}
+
+template <int MaxChunks>
+__device__ __forceinline__ int stream_first_chunk(const StreamArgs<MaxChunks>& a, int64_t t) {
+    int lo = 0, hi = a.n_chunks - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.chunk[mid].tile_begin <= t) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+template <class Op, int MaxChunks>
+__global__ void __launch_bounds__(kStreamThreads, 3) stream_kernel(const __grid_constant__ StreamArgs<MaxChunks> a) {
+    using G = StreamGeometry<Op>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kStages * G::kTileBytes);
+    __shared__ int abort_flag;
+
+    // this CTA's contiguous tile range [t0, t1)
+    const int64_t per = a.total_tiles / gridDim.x, extra = a.total_tiles % gridDim.x;
+    const int64_t b = blockIdx.x;
+    const int64_t t0 = b * per + (b < extra ? b : extra);
+    const int64_t t1 = t0 + per + (b < extra ? 1 : 0);
+    if (t0 >= t1) return;
+
+    int kp = 0;  // producer's chunk cursor (thread 0 only)
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < G::kStages; ++s) mbar_init(&full[s], 1);
+        fence_barrier_init();
+        abort_flag = 0;
+        kp = stream_first_chunk(a, t0);
+    }
+    __syncthreads();
+
+    // Thread 0: start the copy of tile t into stage s (or a bare arrive when
+    // the chunk is unaligned and the consumers read it from global memory).
+    auto issue = [&](int64_t t, int s) {
+        kp = stream_find_chunk(a, t, kp);
+        const ChunkRec& ch = a.chunk[kp];
+        const int64_t e0 = (t - ch.tile_begin) * kTileElems;
+        const int64_t cnt = min(kTileElems, ch.n - e0);
+        const uint32_t bytes = static_cast<uint32_t>((cnt * Op::kIn) & ~int64_t(15));
+        if (ch.aligned && bytes > 0) {
+            mbar_arrive_expect_tx(&full[s], bytes);
+            bulk_g2s(smem + s * G::kTileBytes, static_cast<const uint8_t*>(ch.src) + e0 * Op::kIn, bytes, &full[s]);
+        } else {
+            mbar_arrive(&full[s]);
+        }
+    };
+
+    const int64_t ntiles = t1 - t0;
+    if (threadIdx.x == 0)
+        for (int s = 0; s < G::kStages && s < ntiles; ++s) issue(t0 + s, s);
+
+    int k = stream_first_chunk(a, t0);
+    typename Op::State st = Op::setup(a, a.chunk[k]);
+    int64_t i = 0;
+    for (; i < ntiles; ++i) {
+        const int64_t t = t0 + i;
+        const int s = static_cast<int>(i % G::kStages);
+        const uint32_t parity = static_cast<uint32_t>((i / G::kStages) & 1);
+        if (a.chunk[k].tile_begin + ((a.chunk[k].n + kTileElems - 1) / kTileElems) <= t) {
+            k = stream_find_chunk(a, t, k);
+            st = Op::setup(a, a.chunk[k]);
+        }
+        const ChunkRec& ch = a.chunk[k];
+        const int64_t tile = t - ch.tile_begin;
+        const int64_t e0 = tile * kTileElems;
+        const int64_t cnt = min(kTileElems, ch.n - e0);
+        if (!mbar_wait(&full[s], parity)) abort_flag = 1;
+        if (tile == 0 && threadIdx.x == 0) Op::first_tile(a, ch);
+        if (ch.aligned) {
+            const uint8_t* tp = smem + s * G::kTileBytes;
+            const int nfull = static_cast<int>(cnt / kChunk);
+            const int64_t cbase = e0 / kChunk;
+            for (int c = threadIdx.x; c < nfull; c += kStreamThreads) {
+                RawChunk<Op::kIn> r;
+                load_raw_smem<Op::kIn>(tp, c, r);
+                Op::chunk16(r, ch, cbase + c, st);
+            }
+            const int rem = static_cast<int>(cnt % kChunk);
+            if (threadIdx.x < rem) Op::element(ch, e0 + nfull * kChunk + threadIdx.x, st);
+        } else {
+            for (int64_t j = e0 + threadIdx.x; j < e0 + cnt; j += kStreamThreads) Op::element(ch, j, st);
+        }
+        __syncthreads();  // stage s fully consumed; abort_flag visible
+        if (abort_flag) break;
+        if (threadIdx.x == 0 && i + G::kStages < ntiles) issue(t + G::kStages, s);
+    }
+    if (abort_flag && threadIdx.x == 0) {
+        atomicExch(a.status, kDeviceTimeout);
+        // Let every copy this CTA issued land before its shared memory goes
+        // away: tiles i .. i + kStages - 1 were issued and not consumed.
+        for (int64_t j = i; j < ntiles && j < i + G::kStages; ++j)
+            mbar_wait(&full[j % G::kStages], static_cast<uint32_t>((j / G::kStages) & 1));
+    }
+}
+
+// Host side: launch the engine over a filled argument block.
+int* sticky_status_ptr();
+
+template <class Op, int MaxChunks>
+inline cudaError_t launch_stream(const StreamArgs<MaxChunks>& a, int sm_count, cudaStream_t s) {
+    using G = StreamGeometry<Op>;
+    static int attr_done[64] = {0};  // per device: dynamic shared memory opt-in done
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(stream_kernel<Op, MaxChunks>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes);
+        if (e != cudaSuccess) return e;
+        attr_done[dev] = 1;
+    }
+    int64_t blocks = static_cast<int64_t>(sm_count) * 3;
+    if (a.total_tiles < blocks) blocks = a.total_tiles;
+    if (blocks < 1) return cudaSuccess;
+    stream_kernel<Op, MaxChunks><<<static_cast<unsigned>(blocks), kStreamThreads, G::kSmemBytes, s>>>(a);
+    return cudaGetLastError();
+}
+
+// One flat array as a single-chunk argument block.
+inline void single_chunk(StreamArgs<1>& a, const void* src, void* dst, int64_t n, bool aligned) {
+    a.chunk[0].src = src;
+    a.chunk[0].dst = dst;
+    a.chunk[0].n = n;
+    a.chunk[0].tile_begin = 0;
+    a.chunk[0].tensor = 0;
+    a.chunk[0].aligned = aligned ? 1 : 0;
+    a.n_chunks = 1;
+    a.total_tiles = (n + kTileElems - 1) / kTileElems;
+    a.status = sticky_status_ptr();
+}
+
+}  // namespace mf

@@ -29,23 +29,12 @@
 
 #include "mf_internal.h"
 #include "mf_runtime.h"
-#include "mf_vec.cuh"
+#include "mf_stream.cuh"
 
 namespace mf {
 namespace {
 
 constexpr int kThreads = 256;
-
-__host__ __device__ inline float fp8_max(int fp8_dtype) { return fp8_dtype == MF_DT_F8E5M2 ? 57344.0f : 448.0f; }
-
-__device__ __forceinline__ float scale_from_amax(float amax, int fp8_dtype) {
-    const bool ok = (amax > 0.0f) && (amax < __int_as_float(0x7f800000));
-    return ok ? __fdiv_rn(fp8_max(fp8_dtype), amax) : 1.0f;
-}
-__device__ __forceinline__ float scale_inv_from_amax(float amax, int fp8_dtype) {
-    const bool ok = (amax > 0.0f) && (amax < __int_as_float(0x7f800000));
-    return ok ? __fdiv_rn(amax, fp8_max(fp8_dtype)) : 1.0f;
-}
 
 // ---------------------------------------------------------------- amax
 
@@ -202,50 +191,6 @@ __device__ __forceinline__ uint32_t encode_fp8(float v, int compat) {
     return encode_f32<FP8>(v, compat);
 }
 
-template <int SRC, int FP8, int COMPAT>
-__device__ __forceinline__ void cast_chunk(const void* src, void* dst, int64_t c, float scale) {
-    RawChunk<dtype_bytes(SRC)> r;
-    load_raw<dtype_bytes(SRC)>(src, c, r);
-    float v[kChunk];
-    decode16<SRC>(r, v);
-#pragma unroll
-    for (int k = 0; k < kChunk; ++k) v[k] = __fmul_rn(v[k], scale);
-    RawChunk<1> o;
-    encode16<FP8>(v, o, COMPAT);
-    store_raw<1>(dst, c, o);
-}
-
-template <int SRC, int FP8, int COMPAT>
-__global__ void __launch_bounds__(kThreads) scaled_cast_vec_kernel(const void* __restrict__ src,
-                                                                  void* __restrict__ dst, int64_t n,
-                                                                  const float* __restrict__ d_amax,
-                                                                  float* __restrict__ d_scale_inv) {
-    const float amax = *d_amax;
-    const float scale = scale_from_amax(amax, FP8);
-    if (d_scale_inv && blockIdx.x == 0 && threadIdx.x == 0) *d_scale_inv = scale_inv_from_amax(amax, FP8);
-    const int64_t nchunks = n / kChunk;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nchunks; c += stride)
-        cast_chunk<SRC, FP8, COMPAT>(src, dst, c, scale);
-    if (blockIdx.x == 0) {
-        const int64_t i = nchunks * kChunk + threadIdx.x;
-        if (i < n) store_code<FP8>(dst, i, encode_fp8<FP8>(__fmul_rn(load_as_f32<SRC>(src, i), scale), COMPAT));
-    }
-}
-
-template <int SRC, int FP8>
-__global__ void __launch_bounds__(kThreads) scaled_cast_scalar_kernel(const void* __restrict__ src,
-                                                                     void* __restrict__ dst, int64_t n,
-                                                                     const float* __restrict__ d_amax,
-                                                                     float* __restrict__ d_scale_inv, int compat) {
-    const float amax = *d_amax;
-    const float scale = scale_from_amax(amax, FP8);
-    if (d_scale_inv && blockIdx.x == 0 && threadIdx.x == 0) *d_scale_inv = scale_inv_from_amax(amax, FP8);
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
-        store_code<FP8>(dst, i, encode_fp8<FP8>(__fmul_rn(load_as_f32<SRC>(src, i), scale), compat));
-}
-
 template <int SRC>
 void amax_dispatch(const void* src, int64_t n, float* d_amax, cudaStream_t s) {
     if (aligned16(src)) {
@@ -258,26 +203,21 @@ void amax_dispatch(const void* src, int64_t n, float* d_amax, cudaStream_t s) {
 }
 
 template <int SRC, int FP8>
-void cast_dispatch(const void* src, void* dst, int64_t n, const float* d_amax, float* d_scale_inv, int compat,
-                   cudaStream_t s) {
-    if (aligned16(src) && aligned16(dst)) {
-        const int64_t blocks = stream_grid(n / kChunk + 1, kThreads, 8);
-        if (compat)
-            scaled_cast_vec_kernel<SRC, FP8, 1><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, d_amax, d_scale_inv);
-        else
-            scaled_cast_vec_kernel<SRC, FP8, 0><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, d_amax, d_scale_inv);
-    } else {
-        const int64_t blocks = stream_grid(n, kThreads, 8);
-        scaled_cast_scalar_kernel<SRC, FP8><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, d_amax,
-                                                                                             d_scale_inv, compat);
-    }
+cudaError_t cast_dispatch(const void* src, void* dst, int64_t n, const float* d_amax, float* d_scale_inv, int compat,
+                          cudaStream_t s) {
+    StreamArgs<1> a{};
+    single_chunk(a, src, dst, n, aligned16(src) && aligned16(dst));
+    a.amax = d_amax;
+    a.scale_inv = d_scale_inv;
+    if (compat) return launch_stream<CastOp<SRC, FP8, 1>, 1>(a, state().sm_count, s);
+    return launch_stream<CastOp<SRC, FP8, 0>, 1>(a, state().sm_count, s);
 }
 
 template <int SRC>
-void cast_dispatch_fp8(int fp8_dtype, const void* src, void* dst, int64_t n, const float* d_amax,
-                       float* d_scale_inv, int compat, cudaStream_t s) {
-    if (fp8_dtype == MF_DT_F8E4M3) cast_dispatch<SRC, MF_DT_F8E4M3>(src, dst, n, d_amax, d_scale_inv, compat, s);
-    else cast_dispatch<SRC, MF_DT_F8E5M2>(src, dst, n, d_amax, d_scale_inv, compat, s);
+cudaError_t cast_dispatch_fp8(int fp8_dtype, const void* src, void* dst, int64_t n, const float* d_amax,
+                              float* d_scale_inv, int compat, cudaStream_t s) {
+    if (fp8_dtype == MF_DT_F8E4M3) return cast_dispatch<SRC, MF_DT_F8E4M3>(src, dst, n, d_amax, d_scale_inv, compat, s);
+    return cast_dispatch<SRC, MF_DT_F8E5M2>(src, dst, n, d_amax, d_scale_inv, compat, s);
 }
 
 // ----------------------------------------------------- grouped (ckpt)
@@ -293,25 +233,23 @@ struct Tile {
     static constexpr int64_t kElems = int64_t(kThreads) * kChunks * kChunk;
 };
 
-struct ChunkRec {
+struct AmaxChunk {
     const void* src;
-    void* dst;
     int64_t n;
     int64_t tile_begin;  // first tile of this chunk within the launch
     int32_t tensor;
-    int32_t aligned;     // src and dst 16-byte aligned
+    int32_t aligned;     // src 16-byte aligned
 };
 
-struct GroupArgs {
+struct AmaxArgs {
     float* amax;
-    float* scale_inv;
     int64_t total_tiles;
     int32_t n_chunks;
-    int32_t fp8_dtype;
-    ChunkRec chunk[kGroupMaxChunks];
+    int32_t pad;
+    AmaxChunk chunk[kGroupMaxChunks];
 };
 
-__device__ __forceinline__ int find_chunk(const GroupArgs& a, int64_t t) {
+__device__ __forceinline__ int find_chunk(const AmaxArgs& a, int64_t t) {
     int lo = 0, hi = a.n_chunks - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
@@ -323,7 +261,7 @@ __device__ __forceinline__ int find_chunk(const GroupArgs& a, int64_t t) {
 
 // max|v| over one tile of one chunk (NaN ignored).
 template <int SRC>
-__device__ __forceinline__ float tile_amax(const ChunkRec& ch, int64_t tile) {
+__device__ __forceinline__ float tile_amax(const AmaxChunk& ch, int64_t tile) {
     using T = Tile<SRC>;
     const int64_t c0 = tile * (T::kElems / kChunk);
     const int64_t full = ch.n / kChunk;
@@ -354,43 +292,6 @@ __device__ __forceinline__ float tile_amax(const ChunkRec& ch, int64_t tile) {
     return m;
 }
 
-template <int SRC, int FP8, int COMPAT>
-__device__ __forceinline__ void tile_cast(const ChunkRec& ch, int64_t tile, float scale) {
-    using T = Tile<SRC>;
-    const int64_t c0 = tile * (T::kElems / kChunk);
-    const int64_t full = ch.n / kChunk;
-    if (ch.aligned) {
-        RawChunk<dtype_bytes(SRC)> r[T::kChunks];
-#pragma unroll
-        for (int k = 0; k < T::kChunks; ++k) {
-            const int64_t c = c0 + k * kThreads + threadIdx.x;
-            if (c < full) load_raw<dtype_bytes(SRC)>(ch.src, c, r[k]);
-        }
-#pragma unroll
-        for (int k = 0; k < T::kChunks; ++k) {
-            const int64_t c = c0 + k * kThreads + threadIdx.x;
-            if (c < full) {
-                float v[kChunk];
-                decode16<SRC>(r[k], v);
-#pragma unroll
-                for (int j = 0; j < kChunk; ++j) v[j] = __fmul_rn(v[j], scale);
-                RawChunk<1> o;
-                encode16<FP8>(v, o, COMPAT);
-                store_raw<1>(ch.dst, c, o);
-            }
-        }
-        const int64_t last_tile = (ch.n - 1) / T::kElems;
-        if (tile == last_tile && threadIdx.x < (ch.n % kChunk)) {
-            const int64_t i = full * kChunk + threadIdx.x;
-            store_code<FP8>(ch.dst, i, encode_fp8<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), scale), COMPAT));
-        }
-    } else {
-        const int64_t e0 = tile * T::kElems;
-        for (int64_t i = e0 + threadIdx.x; i < e0 + T::kElems && i < ch.n; i += kThreads)
-            store_code<FP8>(ch.dst, i, encode_fp8<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), scale), COMPAT));
-    }
-}
-
 // This CTA's contiguous tile range [t0, t1).
 __device__ __forceinline__ void tile_range(int64_t total, int64_t& t0, int64_t& t1) {
     const int64_t per = total / gridDim.x, extra = total % gridDim.x;
@@ -400,7 +301,7 @@ __device__ __forceinline__ void tile_range(int64_t total, int64_t& t0, int64_t& 
 }
 
 template <int SRC>
-__global__ void __launch_bounds__(kThreads, 4) group_amax_kernel(const __grid_constant__ GroupArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) group_amax_kernel(const __grid_constant__ AmaxArgs a) {
     int64_t t0, t1;
     tile_range(a.total_tiles, t0, t1);
     if (t0 >= t1) return;
@@ -413,51 +314,48 @@ __global__ void __launch_bounds__(kThreads, 4) group_amax_kernel(const __grid_co
             m = 0.0f;
             ++k;
         }
-        const ChunkRec& ch = a.chunk[k];
+        const AmaxChunk& ch = a.chunk[k];
         m = fmaxf(m, tile_amax<SRC>(ch, t - ch.tile_begin));
     }
     const float bm = block_max(m);
     if (threadIdx.x == 0) atomic_max_nonneg(a.amax + a.chunk[k].tensor, bm);
 }
 
-template <int SRC, int FP8, int COMPAT>
-__global__ void __launch_bounds__(kThreads, 4) group_cast_kernel(const __grid_constant__ GroupArgs a) {
-    int64_t t0, t1;
-    tile_range(a.total_tiles, t0, t1);
-    if (t0 >= t1) return;
-    int k = find_chunk(a, t0);
-    float scale = scale_from_amax(a.amax[a.chunk[k].tensor], FP8);
-    for (int64_t t = t0; t < t1; ++t) {
-        while (k + 1 < a.n_chunks && t >= a.chunk[k + 1].tile_begin) {
-            ++k;
-            scale = scale_from_amax(a.amax[a.chunk[k].tensor], FP8);
-        }
-        const ChunkRec& ch = a.chunk[k];
-        const int64_t tile = t - ch.tile_begin;
-        if (tile == 0 && threadIdx.x == 0 && a.scale_inv)
-            a.scale_inv[ch.tensor] = scale_inv_from_amax(a.amax[ch.tensor], FP8);
-        tile_cast<SRC, FP8, COMPAT>(ch, tile, scale);
-    }
-}
-
-// Fill `a` with the chunks listed in idx[first, first+count); returns the
-// number of tiles of `tile_elems` elements.
-int64_t fill_group(GroupArgs& a, const mf_chunk_desc* chunks, const int32_t* idx, int first, int count,
-                   int64_t tile_elems) {
+// Fill the amax / cast argument blocks with the chunks idx[first, first+count);
+// return the number of tiles.
+int64_t fill_amax(AmaxArgs& a, const mf_chunk_desc* chunks, const int32_t* idx, int first, int count,
+                  int64_t tile_elems) {
     int64_t tiles = 0;
-    int used = 0;
     for (int i = 0; i < count; ++i) {
         const mf_chunk_desc& d = chunks[idx[first + i]];
-        ChunkRec& r = a.chunk[used++];
+        AmaxChunk& r = a.chunk[i];
+        r.src = d.src;
+        r.n = d.n;
+        r.tile_begin = tiles;
+        r.tensor = d.tensor;
+        r.aligned = aligned16(d.src) ? 1 : 0;
+        tiles += (d.n + tile_elems - 1) / tile_elems;
+    }
+    a.n_chunks = count;
+    a.total_tiles = tiles;
+    return tiles;
+}
+
+int64_t fill_cast(StreamArgs<kGroupMaxChunks>& a, const mf_chunk_desc* chunks, const int32_t* idx, int first,
+                  int count) {
+    int64_t tiles = 0;
+    for (int i = 0; i < count; ++i) {
+        const mf_chunk_desc& d = chunks[idx[first + i]];
+        ChunkRec& r = a.chunk[i];
         r.src = d.src;
         r.dst = d.dst;
         r.n = d.n;
         r.tile_begin = tiles;
         r.tensor = d.tensor;
         r.aligned = (aligned16(d.src) && aligned16(d.dst)) ? 1 : 0;
-        tiles += (d.n + tile_elems - 1) / tile_elems;
+        tiles += (d.n + kTileElems - 1) / kTileElems;
     }
-    a.n_chunks = used;
+    a.n_chunks = count;
     a.total_tiles = tiles;
     return tiles;
 }
@@ -481,13 +379,14 @@ int launch_amax(const void* src, int src_dtype, int64_t n, float* d_amax, cudaSt
 int launch_scaled_cast(const void* src, int src_dtype, void* dst, int fp8_dtype, const float* d_amax,
                        float* d_scale_inv, int64_t n, int compat, cudaStream_t s) {
     if (n == 0) return MF_OK;
+    cudaError_t err;
     switch (src_dtype) {
-    case MF_DT_F32: cast_dispatch_fp8<MF_DT_F32>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
-    case MF_DT_F16: cast_dispatch_fp8<MF_DT_F16>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
-    case MF_DT_BF16: cast_dispatch_fp8<MF_DT_BF16>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
+    case MF_DT_F32: err = cast_dispatch_fp8<MF_DT_F32>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
+    case MF_DT_F16: err = cast_dispatch_fp8<MF_DT_F16>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
+    case MF_DT_BF16: err = cast_dispatch_fp8<MF_DT_BF16>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
     default: return fail(MF_ERR_DTYPE_UNSUPPORTED, "scaled cast: source dtype %d unsupported", src_dtype);
     }
-    MF_LAUNCH_CHECK("scaled cast launch");
+    if (err != cudaSuccess) return cuda_fail(err, "scaled cast launch");
     return MF_OK;
 }
 
@@ -581,7 +480,8 @@ static int check_fp8_mode(const char* name, int fp8_dtype, int compat) {
 
 namespace {
 std::mutex g_group_mutex;
-GroupArgs g_group_args;  // ~20 KB; filled under the mutex and copied into the launch
+AmaxArgs g_amax_args;                           // ~16 KB, filled under the mutex
+StreamArgs<kGroupMaxChunks> g_cast_args;        // ~20 KB, filled under the mutex
 
 // Chunk indices with n > 0, grouped by source dtype (BF16, F16, F32), each
 // group in table order.
@@ -595,14 +495,12 @@ void group_by_dtype(const mf_chunk_desc* chunks, int32_t n_chunks, std::vector<i
 
 template <int SRC>
 int amax_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, float* d_amax, cudaStream_t s) {
-    GroupArgs& args = g_group_args;
+    AmaxArgs& args = g_amax_args;
     const int grid_cap = state().sm_count * 8;
     for (int first = 0; first < static_cast<int>(idx.size()); first += kGroupMaxChunks) {
         const int count = std::min<int>(kGroupMaxChunks, static_cast<int>(idx.size()) - first);
         args.amax = d_amax;
-        args.scale_inv = nullptr;
-        args.fp8_dtype = 0;
-        const int64_t tiles = fill_group(args, chunks, idx.data(), first, count, Tile<SRC>::kElems);
+        const int64_t tiles = fill_amax(args, chunks, idx.data(), first, count, Tile<SRC>::kElems);
         if (tiles == 0) continue;
         const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, grid_cap));
         group_amax_kernel<SRC><<<blocks, kThreads, 0, s>>>(args);
@@ -611,27 +509,26 @@ int amax_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, 
     return MF_OK;
 }
 
+template <int SRC, int FP8>
+cudaError_t cast_launch(const StreamArgs<kGroupMaxChunks>& args, int compat, cudaStream_t s) {
+    if (compat) return launch_stream<CastOp<SRC, FP8, 1>, kGroupMaxChunks>(args, state().sm_count, s);
+    return launch_stream<CastOp<SRC, FP8, 0>, kGroupMaxChunks>(args, state().sm_count, s);
+}
+
 template <int SRC>
 int cast_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, const float* d_amax,
                   float* d_scale_inv, int fp8_dtype, int compat, cudaStream_t s) {
-    GroupArgs& args = g_group_args;
-    const int grid_cap = state().sm_count * 8;
+    StreamArgs<kGroupMaxChunks>& args = g_cast_args;
     for (int first = 0; first < static_cast<int>(idx.size()); first += kGroupMaxChunks) {
         const int count = std::min<int>(kGroupMaxChunks, static_cast<int>(idx.size()) - first);
-        args.amax = const_cast<float*>(d_amax);
+        args.amax = d_amax;
         args.scale_inv = d_scale_inv;
-        args.fp8_dtype = fp8_dtype;
-        const int64_t tiles = fill_group(args, chunks, idx.data(), first, count, Tile<SRC>::kElems);
+        args.status = sticky_status_ptr();
+        const int64_t tiles = fill_cast(args, chunks, idx.data(), first, count);
         if (tiles == 0) continue;
-        const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, grid_cap));
-        if (fp8_dtype == MF_DT_F8E4M3) {
-            if (compat) group_cast_kernel<SRC, MF_DT_F8E4M3, 1><<<blocks, kThreads, 0, s>>>(args);
-            else group_cast_kernel<SRC, MF_DT_F8E4M3, 0><<<blocks, kThreads, 0, s>>>(args);
-        } else {
-            if (compat) group_cast_kernel<SRC, MF_DT_F8E5M2, 1><<<blocks, kThreads, 0, s>>>(args);
-            else group_cast_kernel<SRC, MF_DT_F8E5M2, 0><<<blocks, kThreads, 0, s>>>(args);
-        }
-        MF_LAUNCH_CHECK("checkpoint cast pass launch");
+        const cudaError_t err = (fp8_dtype == MF_DT_F8E4M3) ? cast_launch<SRC, MF_DT_F8E4M3>(args, compat, s)
+                                                            : cast_launch<SRC, MF_DT_F8E5M2>(args, compat, s);
+        if (err != cudaSuccess) return cuda_fail(err, "checkpoint cast pass launch");
     }
     return MF_OK;
 }

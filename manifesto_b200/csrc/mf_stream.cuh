@@ -195,7 +195,7 @@ template <class Op>
 struct StreamGeometry {
     static constexpr int kTileBytes = static_cast<int>(kTileElems) * Op::kIn;
     static constexpr int kStages = (kStreamSmemBudget / kTileBytes) < 8 ? (kStreamSmemBudget / kTileBytes) : 8;
-    static constexpr int kSmemBytes = kStages * kTileBytes + kStages * 8;
+    static constexpr int kSmemBytes = kStages * kTileBytes + kStages * 16;
     static_assert(kStages >= 2, "tile too large for the staging budget");
 };
 
@@ -217,12 +217,20 @@ __device__ __forceinline__ int stream_first_chunk(const StreamArgs<MaxChunks>& a
     return lo;
 }
 
+// Warp-specialised pipeline: warps 0..7 consume, warp 8 (one lane) produces.
+//   full[s]  completes when the bulk copy of the tile in stage s has landed
+//            (1 arrival with the byte count, then the transaction bytes);
+//   empty[s] completes when all 8 consumer warps are done with stage s.
+// Consumers never synchronise with each other, only with the copy engine.
+constexpr int kConsumerWarps = kStreamThreads / 32;
+constexpr int kStreamBlock = kStreamThreads + 32;
+
 template <class Op, int MaxChunks>
-__global__ void __launch_bounds__(kStreamThreads, 3) stream_kernel(const __grid_constant__ StreamArgs<MaxChunks> a) {
+__global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_constant__ StreamArgs<MaxChunks> a) {
     using G = StreamGeometry<Op>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kStages * G::kTileBytes);
-    __shared__ int abort_flag;
+    uint64_t* empty = full + G::kStages;
 
     // this CTA's contiguous tile range [t0, t1)
     const int64_t per = a.total_tiles / gridDim.x, extra = a.total_tiles % gridDim.x;
@@ -230,43 +238,59 @@ __global__ void __launch_bounds__(kStreamThreads, 3) stream_kernel(const __grid_
     const int64_t t0 = b * per + (b < extra ? b : extra);
     const int64_t t1 = t0 + per + (b < extra ? 1 : 0);
     if (t0 >= t1) return;
+    const int64_t ntiles = t1 - t0;
 
-    int kp = 0;  // producer's chunk cursor (thread 0 only)
     if (threadIdx.x == 0) {
-        for (int s = 0; s < G::kStages; ++s) mbar_init(&full[s], 1);
+        for (int s = 0; s < G::kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
         fence_barrier_init();
-        abort_flag = 0;
-        kp = stream_first_chunk(a, t0);
     }
     __syncthreads();
 
-    // Thread 0: start the copy of tile t into stage s (or a bare arrive when
-    // the chunk is unaligned and the consumers read it from global memory).
-    auto issue = [&](int64_t t, int s) {
-        kp = stream_find_chunk(a, t, kp);
-        const ChunkRec& ch = a.chunk[kp];
-        const int64_t e0 = (t - ch.tile_begin) * kTileElems;
-        const int64_t cnt = min(kTileElems, ch.n - e0);
-        const uint32_t bytes = static_cast<uint32_t>((cnt * Op::kIn) & ~int64_t(15));
-        if (ch.aligned && bytes > 0) {
-            mbar_arrive_expect_tx(&full[s], bytes);
-            bulk_g2s(smem + s * G::kTileBytes, static_cast<const uint8_t*>(ch.src) + e0 * Op::kIn, bytes, &full[s]);
-        } else {
-            mbar_arrive(&full[s]);
+    if (threadIdx.x >= kStreamThreads) {
+        // ---------------- producer: one lane streams tiles into the ring
+        if (threadIdx.x != kStreamThreads) return;
+        int kp = stream_first_chunk(a, t0);
+        int64_t i = 0;
+        bool ok = true;
+        for (; i < ntiles; ++i) {
+            const int s = static_cast<int>(i % G::kStages);
+            if (i >= G::kStages &&
+                !mbar_wait(&empty[s], static_cast<uint32_t>((i / G::kStages - 1) & 1))) {
+                ok = false;
+                break;
+            }
+            const int64_t t = t0 + i;
+            kp = stream_find_chunk(a, t, kp);
+            const ChunkRec& ch = a.chunk[kp];
+            const int64_t e0 = (t - ch.tile_begin) * kTileElems;
+            const int64_t cnt = min(kTileElems, ch.n - e0);
+            const uint32_t bytes = static_cast<uint32_t>((cnt * Op::kIn) & ~int64_t(15));
+            if (ch.aligned && bytes > 0) {
+                mbar_arrive_expect_tx(&full[s], bytes);
+                bulk_g2s(smem + s * G::kTileBytes, static_cast<const uint8_t*>(ch.src) + e0 * Op::kIn, bytes,
+                         &full[s]);
+            } else {
+                mbar_arrive(&full[s]);  // consumers read this tile from global memory
+            }
         }
-    };
+        if (!ok) atomicExch(a.status, kDeviceTimeout);
+        // Every copy issued must land before the CTA's shared memory goes away:
+        // wait (bounded) for the last kStages issued tiles.
+        for (int64_t j = (i > G::kStages ? i - G::kStages : 0); j < i; ++j)
+            mbar_wait(&full[j % G::kStages], static_cast<uint32_t>((j / G::kStages) & 1));
+        return;
+    }
 
-    const int64_t ntiles = t1 - t0;
-    if (threadIdx.x == 0)
-        for (int s = 0; s < G::kStages && s < ntiles; ++s) issue(t0 + s, s);
-
+    // -------------------- consumers: decode, compute, store
+    const int lane = threadIdx.x & 31;
     int k = stream_first_chunk(a, t0);
     typename Op::State st = Op::setup(a, a.chunk[k]);
-    int64_t i = 0;
-    for (; i < ntiles; ++i) {
+    for (int64_t i = 0; i < ntiles; ++i) {
         const int64_t t = t0 + i;
         const int s = static_cast<int>(i % G::kStages);
-        const uint32_t parity = static_cast<uint32_t>((i / G::kStages) & 1);
         if (a.chunk[k].tile_begin + ((a.chunk[k].n + kTileElems - 1) / kTileElems) <= t) {
             k = stream_find_chunk(a, t, k);
             st = Op::setup(a, a.chunk[k]);
@@ -275,7 +299,10 @@ __global__ void __launch_bounds__(kStreamThreads, 3) stream_kernel(const __grid_
         const int64_t tile = t - ch.tile_begin;
         const int64_t e0 = tile * kTileElems;
         const int64_t cnt = min(kTileElems, ch.n - e0);
-        if (!mbar_wait(&full[s], parity)) abort_flag = 1;
+        if (!mbar_wait(&full[s], static_cast<uint32_t>((i / G::kStages) & 1))) {
+            atomicExch(a.status, kDeviceTimeout);
+            return;  // the producer's own bounded waits end the CTA
+        }
         if (tile == 0 && threadIdx.x == 0) Op::first_tile(a, ch);
         if (ch.aligned) {
             const uint8_t* tp = smem + s * G::kTileBytes;
@@ -291,16 +318,8 @@ __global__ void __launch_bounds__(kStreamThreads, 3) stream_kernel(const __grid_
         } else {
             for (int64_t j = e0 + threadIdx.x; j < e0 + cnt; j += kStreamThreads) Op::element(ch, j, st);
         }
-        __syncthreads();  // stage s fully consumed; abort_flag visible
-        if (abort_flag) break;
-        if (threadIdx.x == 0 && i + G::kStages < ntiles) issue(t + G::kStages, s);
-    }
-    if (abort_flag && threadIdx.x == 0) {
-        atomicExch(a.status, kDeviceTimeout);
-        // Let every copy this CTA issued land before its shared memory goes
-        // away: tiles i .. i + kStages - 1 were issued and not consumed.
-        for (int64_t j = i; j < ntiles && j < i + G::kStages; ++j)
-            mbar_wait(&full[j % G::kStages], static_cast<uint32_t>((j / G::kStages) & 1));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
     }
 }
 
@@ -322,7 +341,7 @@ inline cudaError_t launch_stream(const StreamArgs<MaxChunks>& a, int sm_count, c
     int64_t blocks = static_cast<int64_t>(sm_count) * 3;
     if (a.total_tiles < blocks) blocks = a.total_tiles;
     if (blocks < 1) return cudaSuccess;
-    stream_kernel<Op, MaxChunks><<<static_cast<unsigned>(blocks), kStreamThreads, G::kSmemBytes, s>>>(a);
+    stream_kernel<Op, MaxChunks><<<static_cast<unsigned>(blocks), kStreamBlock, G::kSmemBytes, s>>>(a);
     return cudaGetLastError();
 }
 

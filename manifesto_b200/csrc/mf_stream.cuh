@@ -133,12 +133,14 @@ struct ConvertOp {
     __device__ static State setup(const A&, const ChunkRec&) { return {}; }
     template <class A>
     __device__ static void first_tile(const A&, const ChunkRec&) {}
-    __device__ static void chunk16(const RawChunk<kIn>& r, const ChunkRec& ch, int64_t c, const State&) {
-        float v[kChunk];
-        decode16<SRC>(r, v);
-        RawChunk<dtype_bytes(DST)> o;
-        encode16<DST>(v, o, COMPAT);
-        store_raw<dtype_bytes(DST)>(ch.dst, c, o);
+    // elements e .. e+3 of the chunk; their source bytes are at sp (shared memory)
+    __device__ static void quad(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State&) {
+        uint32_t w[kIn], o[dtype_bytes(DST)];
+        load4<kIn>(sp, w);
+        float v[4];
+        decode4<SRC>(w, v);
+        encode4<DST>(v, o, COMPAT);
+        store4_stream<dtype_bytes(DST)>(static_cast<uint8_t*>(ch.dst) + e * dtype_bytes(DST), o);
     }
     __device__ static void element(const ChunkRec& ch, int64_t i, const State&) {
         store_code<DST>(ch.dst, i, encode_f32<DST>(load_as_f32<SRC>(ch.src, i), COMPAT));
@@ -171,18 +173,16 @@ struct CastOp {
     __device__ static void first_tile(const A& a, const ChunkRec& ch) {
         if (a.scale_inv) a.scale_inv[ch.tensor] = scale_inv_from_amax(a.amax[ch.tensor], FP8);
     }
-    __device__ static void chunk16(const RawChunk<kIn>& r, const ChunkRec& ch, int64_t c, const State& st) {
-        float v[kChunk];
-        decode16<SRC>(r, v);
-#pragma unroll
-        for (int k = 0; k < kChunk; k += 2) {
-            const float2 p = __fmul2_rn(make_float2(v[k], v[k + 1]), make_float2(st.scale, st.scale));
-            v[k] = p.x;
-            v[k + 1] = p.y;
-        }
-        RawChunk<1> o;
-        encode16<FP8>(v, o, COMPAT);
-        store_raw<1>(ch.dst, c, o);
+    __device__ static void quad(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State& st) {
+        uint32_t w[kIn], o[1];
+        load4<kIn>(sp, w);
+        float v[4];
+        decode4<SRC>(w, v);
+        const float2 a = __fmul2_rn(make_float2(v[0], v[1]), make_float2(st.scale, st.scale));
+        const float2 b = __fmul2_rn(make_float2(v[2], v[3]), make_float2(st.scale, st.scale));
+        const float s[4] = {a.x, a.y, b.x, b.y};
+        encode4<FP8>(s, o, COMPAT);
+        store4_stream<1>(static_cast<uint8_t*>(ch.dst) + e, o);
     }
     __device__ static void element(const ChunkRec& ch, int64_t i, const State& st) {
         store_code<FP8>(ch.dst, i, encode_f32<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), st.scale), COMPAT));
@@ -305,16 +305,16 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
         }
         if (tile == 0 && threadIdx.x == 0) Op::first_tile(a, ch);
         if (ch.aligned) {
+            // lane-consecutive quads: every warp access is one contiguous span
+            // only the first ((cnt * kIn) & ~15) bytes were copied (16-byte
+            // granularity); the elements past them come from global memory
             const uint8_t* tp = smem + s * G::kTileBytes;
-            const int nfull = static_cast<int>(cnt / kChunk);
-            const int64_t cbase = e0 / kChunk;
-            for (int c = threadIdx.x; c < nfull; c += kStreamThreads) {
-                RawChunk<Op::kIn> r;
-                load_raw_smem<Op::kIn>(tp, c, r);
-                Op::chunk16(r, ch, cbase + c, st);
-            }
-            const int rem = static_cast<int>(cnt % kChunk);
-            if (threadIdx.x < rem) Op::element(ch, e0 + nfull * kChunk + threadIdx.x, st);
+            const int copied = static_cast<int>(((cnt * Op::kIn) & ~int64_t(15)) / Op::kIn);
+            const int nquads = copied / 4;
+            for (int q = threadIdx.x; q < nquads; q += kStreamThreads)
+                Op::quad(tp + q * 4 * Op::kIn, ch, e0 + 4 * q, st);
+            const int rem = static_cast<int>(cnt) - nquads * 4;
+            if (threadIdx.x < rem) Op::element(ch, e0 + nquads * 4 + threadIdx.x, st);
         } else {
             for (int64_t j = e0 + threadIdx.x; j < e0 + cnt; j += kStreamThreads) Op::element(ch, j, st);
         }

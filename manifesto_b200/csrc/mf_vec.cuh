@@ -1,12 +1,15 @@
-// mf_vec.cuh -- 128-bit streaming access to 16-element chunks.
+// mf_vec.cuh -- vector access and packed codecs for the streaming kernels.
 //
-// Every streaming kernel in this library moves data in chunks of 16
-// logical elements: 16 B of an 8-bit format, 32 B of a 16-bit format, 64 B
-// of float32.  A chunk is read with one to four 128-bit loads (LDG.128)
-// and written with one to four 128-bit stores, so a warp touches whole
-// 512 B..2 KB contiguous segments per access.  Inputs are read with the
-// non-coherent path and the evict-first hint (each byte is read once);
-// outputs are written with the streaming store hint.
+// Two granularities:
+//   * chunks of 16 elements (16 B of an 8-bit format, 32 B of a 16-bit
+//     format, 64 B of float32) read with one to four 128-bit loads, used by
+//     kernels whose per-thread work is naturally 16 elements (the Int4
+//     dequant, the amax folds);
+//   * quads of 4 elements, owned by consecutive lanes so every warp-wide
+//     access is one contiguous span whatever the element widths, used by the
+//     element-wise maps (conversion, casts, axpy).
+// Inputs are read with the non-coherent path and the evict-first hint (each
+// byte is read once); outputs are written with the streaming store hint.
 #pragma once
 
 #include "mf_numerics.cuh"
@@ -152,80 +155,166 @@ __device__ __forceinline__ uint32_t cvt4_fp8_satfinite(float v0, float v1, float
     return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
 }
 
-// NaN lanes (magnitude 0x7f) -> 0x7f without sign, four bytes at a time.
-__device__ __forceinline__ uint32_t fp8x4_canonical_nan(uint32_t w, uint32_t nan_mag4) {
-    const uint32_t nan = __vcmpgeu4(w & 0x7f7f7f7fu, nan_mag4);
+// NaN lanes -> 0x7f without sign, four bytes at a time.  A byte is NaN when
+// its magnitude plus `add4`'s byte carries into bit 7: add 0x01 for E4M3
+// (NaN magnitude 0x7f), 0x03 for E5M2 (NaN magnitudes 0x7d..0x7f).
+__device__ __forceinline__ uint32_t fp8x4_canonical_nan(uint32_t w, uint32_t add4) {
+    const uint32_t hi = ((w & 0x7f7f7f7fu) + add4) & 0x80808080u;
+    const uint32_t nan = hi | (hi - (hi >> 7));
     return (w & ~nan) | (nan & 0x7f7f7f7fu);
 }
 
-// E4M3 encode of 16 values with the reference's rules (dtype/fp8.go:77-136),
-// fast path: the hardware .satfinite conversion agrees with the reference
-// everywhere except (a) |v| >= 248, where the reference saturates to 0x7e
-// (exponent 15 is never produced), (b) NaN, always 0x7f, and (c) the
-// subnormal band 2^-10 <= |v| < 2^-6, where the reference's shift differs.
-// (a) and (b) are fixed on the packed codes with byte-SIMD compares; a chunk
-// with any element in band (c) is re-encoded with the exact integer routine.
-__device__ __forceinline__ void encode16_e4m3_ref(const float (&v)[kChunk], uint32_t (&w)[4]) {
-    uint32_t band = 0;
-#pragma unroll
-    for (int k = 0; k < kChunk; ++k)
-        band |= static_cast<uint32_t>(((__float_as_uint(v[k]) & 0x7fffffffu) - 0x3a800000u) < 0x02000000u);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        uint32_t c = cvt4_fp8_satfinite<MF_DT_F8E4M3>(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-        // .satfinite yields magnitude 0x7f (S.1111.111) only for NaN inputs
-        const uint32_t m7 = c & 0x7f7f7f7fu;
-        const uint32_t nan = __vcmpeq4(m7, 0x7f7f7f7fu);
-        const uint32_t big = __vcmpgeu4(m7, 0x78787878u);  // |v| >= 248
-        c = (c & ~big) | (big & ((c & 0x80808080u) | 0x7e7e7e7eu));
-        w[k] = (c & ~nan) | (nan & 0x7f7f7f7fu);
+// ------------------------------------------------------------ quads
+//
+// A quad is 4 consecutive elements owned by one lane; lane l of a warp owns
+// quad q0 + l, so one warp-wide access covers 128 consecutive elements
+// (128..512 contiguous bytes) and every vector load and store is fully
+// coalesced whatever the element widths on the two sides.
+
+// Byte-wise mask: 0xff in every byte whose bit 7 is set in `hi` (other bits 0).
+__device__ __forceinline__ uint32_t bytes_from_bit7(uint32_t hi) { return hi | (hi - (hi >> 7)); }
+
+// Four float32 -> four E4M3 codes with the reference's rules
+// (dtype/fp8.go:77-136).  The hardware .satfinite conversion agrees with the
+// reference except (a) |v| >= 248, which the reference saturates to 0x7e
+// (hardware codes 0x78..0x7e, fixed with a byte mask), and (b) the
+// reference's subnormal band 2^-10 <= |v| < 2^-6, (c) NaN -> 0x7f.  Band
+// values get hardware codes 1..8, or 0 for exactly 2^-10; NaN gets 0x7f.
+// A quad holding any of those is re-encoded with the exact integer routine.
+__device__ __forceinline__ uint32_t encode4_e4m3_ref(float v0, float v1, float v2, float v3) {
+    const uint32_t c = cvt4_fp8_satfinite<MF_DT_F8E4M3>(v0, v1, v2, v3);
+    const uint32_t c7 = c & 0x7f7f7f7fu;
+    const uint32_t big = bytes_from_bit7((c7 + 0x08080808u) & 0x80808080u);  // code >= 0x78
+    uint32_t res = (c & ~big) | (big & ((c & 0x80808080u) | 0x7e7e7e7eu));
+    const uint32_t y = ((c7 + 0x77777777u) ^ 0x78787878u) & 0xf8f8f8f8u;      // zero byte: code in [1, 8]
+    uint32_t special = ((y - 0x01010101u) & ~y & 0x80808080u) | ((c7 + 0x01010101u) & 0x80808080u);
+    if ((c7 - 0x01010101u) & ~c7 & 0x80808080u) {  // some code is 0: is it exactly 2^-10?
+        special |= (fabsf(v0) == 0.0009765625f) | (fabsf(v1) == 0.0009765625f) | (fabsf(v2) == 0.0009765625f) |
+                   (fabsf(v3) == 0.0009765625f);
     }
-    if (band) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            uint32_t c = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) c |= f32bits_to_e4m3_ref(__float_as_uint(v[4 * k + j])) << (8 * j);
-            w[k] = c;
-        }
+    if (special) {
+        res = f32bits_to_e4m3_ref(__float_as_uint(v0)) | (f32bits_to_e4m3_ref(__float_as_uint(v1)) << 8) |
+              (f32bits_to_e4m3_ref(__float_as_uint(v2)) << 16) | (f32bits_to_e4m3_ref(__float_as_uint(v3)) << 24);
     }
+    return res;
 }
 
-// E5M2 encode of 16 values with the reference's rules (dtype/fp8.go:190-249):
-// the hardware result is kept unless the chunk holds a value in the
-// reference's subnormal band 2^-17 <= |v| < 2^-14, a value above 57344
-// (the reference returns Inf there) or a NaN; such chunks take the exact
-// integer routine.
-__device__ __forceinline__ void encode16_e5m2_ref(const float (&v)[kChunk], uint32_t (&w)[4]) {
-    uint32_t slow = 0;
+// Four float32 -> four E5M2 codes with the reference's rules
+// (dtype/fp8.go:190-249): the hardware result unless a value lies in the
+// reference's subnormal band 2^-17 <= |v| < 2^-14, above 57344 (the
+// reference returns Inf) or is NaN; then the exact integer routine.
+__device__ __forceinline__ uint32_t encode4_e5m2_ref(float v0, float v1, float v2, float v3) {
+    const float a[4] = {fabsf(v0), fabsf(v1), fabsf(v2), fabsf(v3)};
+    bool slow = false;
 #pragma unroll
-    for (int k = 0; k < kChunk; ++k) {
-        const uint32_t a = __float_as_uint(v[k]) & 0x7fffffffu;
-        slow |= static_cast<uint32_t>((a - 0x37000000u) < 0x01800000u) | static_cast<uint32_t>(a > 0x47600000u);
-    }
-    if (slow) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            uint32_t c = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) c |= f32bits_to_e5m2_ref(__float_as_uint(v[4 * k + j])) << (8 * j);
-            w[k] = c;
-        }
-    } else {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) w[k] = cvt4_fp8_satfinite<MF_DT_F8E5M2>(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-    }
+    for (int j = 0; j < 4; ++j)
+        slow |= ((a[j] >= 7.62939453125e-06f) & (a[j] < 6.103515625e-05f)) | !(a[j] <= 57344.0f);
+    if (slow)
+        return f32bits_to_e5m2_ref(__float_as_uint(v0)) | (f32bits_to_e5m2_ref(__float_as_uint(v1)) << 8) |
+               (f32bits_to_e5m2_ref(__float_as_uint(v2)) << 16) | (f32bits_to_e5m2_ref(__float_as_uint(v3)) << 24);
+    return cvt4_fp8_satfinite<MF_DT_F8E5M2>(v0, v1, v2, v3);
 }
 
-// OCP .satfinite encode of 16 values with NaN -> 0x7f.  .satfinite never
-// produces Inf, so a code magnitude of 0x7f (E4M3) or >= 0x7d (E5M2) is NaN.
+// Decode one quad (raw words w[0 .. bytes-1]) of a floating storage format.
 template <int DT>
-__device__ __forceinline__ void encode16_fp8_ocp(const float (&v)[kChunk], uint32_t (&w)[4]) {
-    constexpr uint32_t kNanMag = (DT == MF_DT_F8E4M3) ? 0x7f7f7f7fu : 0x7d7d7d7du;
+__device__ __forceinline__ void decode4(const uint32_t* w, float (&v)[4]) {
+    if constexpr (DT == MF_DT_F32) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-        w[k] = fp8x4_canonical_nan(cvt4_fp8_satfinite<DT>(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]),
-                                   kNanMag);
+        for (int k = 0; k < 4; ++k) v[k] = __uint_as_float(w[k]);
+    } else if constexpr (DT == MF_DT_BF16) {
+        v[0] = __uint_as_float(w[0] << 16);
+        v[1] = __uint_as_float(w[0] & 0xffff0000u);
+        v[2] = __uint_as_float(w[1] << 16);
+        v[3] = __uint_as_float(w[1] & 0xffff0000u);
+    } else if constexpr (DT == MF_DT_F16) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            f16x2_to_f32x2(w[k], v[2 * k], v[2 * k + 1]);
+            if (((w[k] & 0x7fff7fffu) + 0x03ff03ffu) & 0x80008000u) {
+                v[2 * k] = __uint_as_float(f16_to_f32bits(w[k] & 0xffffu));
+                v[2 * k + 1] = __uint_as_float(f16_to_f32bits(w[k] >> 16));
+            }
+        }
+    } else if constexpr (DT == MF_DT_F8E4M3) {
+        f16x2_to_f32x2(e4m3x2_to_f16x2(w[0]), v[0], v[1]);
+        f16x2_to_f32x2(e4m3x2_to_f16x2(w[0] >> 16), v[2], v[3]);
+        const uint32_t x = ~w[0] & 0x7f7f7f7fu;
+        if ((x - 0x01010101u) & ~x & 0x80808080u) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = __uint_as_float(e4m3_to_f32bits((w[0] >> (8 * j)) & 0xffu));
+        }
+    } else if constexpr (DT == MF_DT_F8E5M2) {
+        f16x2_to_f32x2(__byte_perm(w[0], 0u, 0x1404u), v[0], v[1]);
+        f16x2_to_f32x2(__byte_perm(w[0], 0u, 0x3424u), v[2], v[3]);
+        if (((w[0] & 0x7f7f7f7fu) + 0x03030303u) & 0x80808080u) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = __uint_as_float(e5m2_to_f32bits((w[0] >> (8 * j)) & 0xffu));
+        }
+    }
+}
+
+// Encode one quad to raw words o[0 .. bytes-1].
+template <int DT>
+__device__ __forceinline__ void encode4(const float (&v)[4], uint32_t* o, int compat) {
+    if constexpr (DT == MF_DT_F32) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] = __float_as_uint(v[k]);
+    } else if constexpr (DT == MF_DT_BF16) {
+        o[0] = f32x2_to_bf16x2(v[0], v[1]);
+        o[1] = f32x2_to_bf16x2(v[2], v[3]);
+    } else if constexpr (DT == MF_DT_F16) {
+        o[0] = f32x2_to_f16x2(v[0], v[1]);
+        o[1] = f32x2_to_f16x2(v[2], v[3]);
+    } else if constexpr (DT == MF_DT_F8E4M3) {
+        o[0] = compat ? fp8x4_canonical_nan(cvt4_fp8_satfinite<DT>(v[0], v[1], v[2], v[3]), 0x01010101u)
+                      : encode4_e4m3_ref(v[0], v[1], v[2], v[3]);
+    } else if constexpr (DT == MF_DT_F8E5M2) {
+        o[0] = compat ? fp8x4_canonical_nan(cvt4_fp8_satfinite<DT>(v[0], v[1], v[2], v[3]), 0x03030303u)
+                      : encode4_e5m2_ref(v[0], v[1], v[2], v[3]);
+    }
+}
+
+// Quad-sized vector access: 4 elements of `Bytes` each.
+template <int Bytes>
+__device__ __forceinline__ void load4(const void* p, uint32_t* w) {
+    if constexpr (Bytes == 1) {
+        w[0] = *static_cast<const uint32_t*>(p);
+    } else if constexpr (Bytes == 2) {
+        const uint2 x = *static_cast<const uint2*>(p);
+        w[0] = x.x;
+        w[1] = x.y;
+    } else {
+        const uint4 x = *static_cast<const uint4*>(p);
+        w[0] = x.x;
+        w[1] = x.y;
+        w[2] = x.z;
+        w[3] = x.w;
+    }
+}
+
+template <int Bytes>
+__device__ __forceinline__ void store4_stream(void* p, const uint32_t* w) {
+    if constexpr (Bytes == 1) {
+        asm volatile("st.global.cs.u32 [%0], %1;" ::"l"(p), "r"(w[0]) : "memory");
+    } else if constexpr (Bytes == 2) {
+        asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(w[0]), "r"(w[1]) : "memory");
+    } else {
+        asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                     : "memory");
+    }
+}
+
+template <int Bytes>
+__device__ __forceinline__ void load4_stream(const void* p, uint32_t* w) {
+    if constexpr (Bytes == 1) {
+        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(w[0]) : "l"(p));
+    } else if constexpr (Bytes == 2) {
+        asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "l"(p));
+    } else {
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                     : "l"(p));
+    }
 }
 
 // Encode 16 float32 values to a storage format.
@@ -240,12 +329,12 @@ __device__ __forceinline__ void encode16(const float (&v)[kChunk], RawChunk<dtyp
     } else if constexpr (DT == MF_DT_F16) {
 #pragma unroll
         for (int k = 0; k < kChunk / 2; ++k) r.w[k] = f32x2_to_f16x2(v[2 * k], v[2 * k + 1]);
-    } else if constexpr (DT == MF_DT_F8E4M3) {
-        if (compat) encode16_fp8_ocp<DT>(v, r.w);
-        else encode16_e4m3_ref(v, r.w);
-    } else if constexpr (DT == MF_DT_F8E5M2) {
-        if (compat) encode16_fp8_ocp<DT>(v, r.w);
-        else encode16_e5m2_ref(v, r.w);
+    } else if constexpr (DT == MF_DT_F8E4M3 || DT == MF_DT_F8E5M2) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float q[4] = {v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]};
+            encode4<DT>(q, &r.w[k], compat);
+        }
     }
 }
 

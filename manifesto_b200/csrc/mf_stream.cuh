@@ -309,12 +309,22 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
             // only the first ((cnt * kIn) & ~15) bytes were copied (16-byte
             // granularity); the elements past them come from global memory
             const uint8_t* tp = smem + s * G::kTileBytes;
-            const int copied = static_cast<int>(((cnt * Op::kIn) & ~int64_t(15)) / Op::kIn);
-            const int nquads = copied / 4;
-            for (int q = threadIdx.x; q < nquads; q += kStreamThreads)
-                Op::quad(tp + q * 4 * Op::kIn, ch, e0 + 4 * q, st);
-            const int rem = static_cast<int>(cnt) - nquads * 4;
-            if (threadIdx.x < rem) Op::element(ch, e0 + nquads * 4 + threadIdx.x, st);
+            if (cnt == kTileElems) {
+                // full tile: a fixed trip count, unrolled
+                constexpr int kQuadsPerThread = static_cast<int>(kTileElems / 4 / kStreamThreads);
+#pragma unroll
+                for (int j = 0; j < kQuadsPerThread; ++j) {
+                    const int q = threadIdx.x + j * kStreamThreads;
+                    Op::quad(tp + q * 4 * Op::kIn, ch, e0 + 4 * q, st);
+                }
+            } else {
+                const int copied = static_cast<int>(((cnt * Op::kIn) & ~int64_t(15)) / Op::kIn);
+                const int nquads = copied / 4;
+                for (int q = threadIdx.x; q < nquads; q += kStreamThreads)
+                    Op::quad(tp + q * 4 * Op::kIn, ch, e0 + 4 * q, st);
+                const int rem = static_cast<int>(cnt) - nquads * 4;
+                if (threadIdx.x < rem) Op::element(ch, e0 + nquads * 4 + threadIdx.x, st);
+            }
         } else {
             for (int64_t j = e0 + threadIdx.x; j < e0 + cnt; j += kStreamThreads) Op::element(ch, j, st);
         }

@@ -181,21 +181,38 @@ __device__ __forceinline__ uint32_t bytes_from_bit7(uint32_t hi) { return hi | (
 // reference's subnormal band 2^-10 <= |v| < 2^-6, (c) NaN -> 0x7f.  Band
 // values get hardware codes 1..8, or 0 for exactly 2^-10; NaN gets 0x7f.
 // A quad holding any of those is re-encoded with the exact integer routine.
+//
+// In the band the reference computes min(8, RNE(|v| * 2^10)) (its shift is
+// one short), which is the hardware code of 2v clamped to 8.  So a quad with
+// a band value is fixed with a second hardware conversion and byte masks;
+// only a NaN or a value of exactly 2^-10 (the hardware rounds that tie to 0,
+// the reference to 1) falls back to the scalar routine.
+static __device__ __noinline__ uint32_t e4m3_ref_low(uint32_t res, uint32_t c, float v0, float v1, float v2,
+                                                     float v3) {
+    const uint32_t c7 = c & 0x7f7f7f7fu;
+    const bool nan = ((c7 + 0x01010101u) & 0x80808080u) != 0;
+    const bool tie = (fabsf(v0) == 0.0009765625f) | (fabsf(v1) == 0.0009765625f) | (fabsf(v2) == 0.0009765625f) |
+                     (fabsf(v3) == 0.0009765625f);
+    if (nan | tie)
+        return f32bits_to_e4m3_ref(__float_as_uint(v0)) | (f32bits_to_e4m3_ref(__float_as_uint(v1)) << 8) |
+               (f32bits_to_e4m3_ref(__float_as_uint(v2)) << 16) | (f32bits_to_e4m3_ref(__float_as_uint(v3)) << 24);
+    // band lanes: hardware code in [1, 8] (y has a zero byte exactly there)
+    const uint32_t y = ((c7 + 0x77777777u) ^ 0x78787878u) & 0xf8f8f8f8u;
+    const uint32_t band = bytes_from_bit7(~(((y & 0x7f7f7f7fu) + 0x7f7f7f7fu) | y) & 0x80808080u);
+    const uint32_t c2 = cvt4_fp8_satfinite<MF_DT_F8E4M3>(v0 + v0, v1 + v1, v2 + v2, v3 + v3) & 0x7f7f7f7fu;
+    const uint32_t ge8 = bytes_from_bit7((c2 + 0x78787878u) & 0x80808080u);
+    const uint32_t low = (c2 & ~ge8) | (0x08080808u & ge8) | (c & 0x80808080u);
+    return (res & ~band) | (low & band);
+}
+
 __device__ __forceinline__ uint32_t encode4_e4m3_ref(float v0, float v1, float v2, float v3) {
     const uint32_t c = cvt4_fp8_satfinite<MF_DT_F8E4M3>(v0, v1, v2, v3);
     const uint32_t c7 = c & 0x7f7f7f7fu;
     const uint32_t big = bytes_from_bit7((c7 + 0x08080808u) & 0x80808080u);  // code >= 0x78
-    uint32_t res = (c & ~big) | (big & ((c & 0x80808080u) | 0x7e7e7e7eu));
-    const uint32_t y = ((c7 + 0x77777777u) ^ 0x78787878u) & 0xf8f8f8f8u;      // zero byte: code in [1, 8]
-    uint32_t special = ((y - 0x01010101u) & ~y & 0x80808080u) | ((c7 + 0x01010101u) & 0x80808080u);
-    if ((c7 - 0x01010101u) & ~c7 & 0x80808080u) {  // some code is 0: is it exactly 2^-10?
-        special |= (fabsf(v0) == 0.0009765625f) | (fabsf(v1) == 0.0009765625f) | (fabsf(v2) == 0.0009765625f) |
-                   (fabsf(v3) == 0.0009765625f);
-    }
-    if (special) {
-        res = f32bits_to_e4m3_ref(__float_as_uint(v0)) | (f32bits_to_e4m3_ref(__float_as_uint(v1)) << 8) |
-              (f32bits_to_e4m3_ref(__float_as_uint(v2)) << 16) | (f32bits_to_e4m3_ref(__float_as_uint(v3)) << 24);
-    }
+    const uint32_t res = (c & ~big) | (big & ((c & 0x80808080u) | 0x7e7e7e7eu));
+    // any code in [0, 8] or 0x7f: (code + 1) mod 128 < 10
+    const uint32_t t = ((c7 + 0x01010101u) & 0x7f7f7f7fu) + 0x76767676u;
+    if (~t & 0x80808080u) return e4m3_ref_low(res, c, v0, v1, v2, v3);
     return res;
 }
 

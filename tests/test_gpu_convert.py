@@ -67,6 +67,31 @@ def test_quirk_bands_dense(backend, ref, dst):
                                                                      threads=host_threads()))
 
 
+def test_fp8_encode_edge_values(backend, ref, golden):
+    """Band edges, the 2^-10 tie, saturation edges, NaN/Inf, in every lane position of a quad."""
+    f32 = lambda x: int(np.array([x], np.float32).view(np.uint32)[0])
+    base = [2.0 ** -10, 2.0 ** -11, 2.0 ** -9, 2.0 ** -7, 2.0 ** -6, 1.5 * 2 ** -10, 248.0, 247.99998, 256.0, 448.0,
+            449.0, 464.0, 57344.0, 57345.0, 61440.0, 2.0 ** -14, 2.0 ** -16, 2.0 ** -17, 1.0, 0.0]
+    vals = [f32(v) for v in base] + [f32(-v) for v in base]
+    vals += [v + d for v in vals for d in (1, 0xFFFFFFFF)]  # one ulp either side (wraps harmlessly)
+    vals += [0x7FC00000, 0xFFC00000, 0x7F800001, 0x7F800000, 0xFF800000, 0x00000001, 0x80000001]
+    vals += [int(c["in"]) for c in golden["known_answers"]["e4m3_encode"]]
+    v = np.array([x & 0xFFFFFFFF for x in vals], np.uint32)
+    # every value in every quad lane, next to band / ordinary / zero neighbours
+    fill = np.array([f32(1.0), f32(2.0 ** -8), 0, f32(300.0)], np.uint32)
+    rows = []
+    for x in v:
+        for lane in range(4):
+            for f in fill:
+                q = np.full(4, f, np.uint32)
+                q[lane] = x
+                rows.append(q)
+    b = np.concatenate(rows)
+    for dst in (E4M3, E5M2):
+        for compat in (0, 1):
+            bits_equal(convert(b, F32, dst, b.size, compat), ref.convert(b, F32, dst, compat=compat))
+
+
 @pytest.mark.parametrize("n", [0, 1, 15, 16, 17, 4095, (1 << 20) + 3])
 @pytest.mark.parametrize("pair", [(E4M3, F32), (BF16, E4M3), (F32, BF16), (F16, F32)])
 def test_ragged_sizes(backend, ref, n, pair):

@@ -329,6 +329,22 @@ int mf_ckpt_quant_fp8(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_t
                       float* d_amax, float* d_scale_inv, int fp8_dtype, int compat,
                       mf_comm comm, mf_stream stream);
 
+/* No counterpart in the reference.  The same quantisation as
+ * mf_ckpt_quant_fp8 for callers that cannot provide device memory for the
+ * per-tensor amax vector -- for example a host whose device memory all
+ * belongs to another allocator, such as an executor that only holds the
+ * workspace arena its graph planner sized in advance, or a deployment that
+ * forbids cudaMalloc after set-up.  The amax vector lives in a static device
+ * array inside the library instead (at most 4096 tensors, 16 KB per GPU,
+ * held until the process exits); larger n_tensors return
+ * MF_ERR_ALLOCATOR_EXHAUSTED.  Nothing is allocated.  Every call on a device
+ * shares that array, so calls that overlap on the GPU race; each call zeroes
+ * the entries it uses.  The first call on a device looks the array up with
+ * that device current; make it before any stream capture. */
+int mf_ckpt_quant_fp8_noalloc(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors,
+                              float* d_scale_inv, int fp8_dtype, int compat, mf_comm comm,
+                              mf_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -590,3 +590,154 @@ extern "C" int mf_ckpt_quant_fp8(const mf_chunk_desc* chunks, int32_t n_chunks, 
     }
     return launch_cast_pass(chunks, n_chunks, d_amax, d_scale_inv, fp8_dtype, compat, s);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free checkpoint quantisation (mf_ckpt_quant_fp8_noalloc).
+//
+// Some callers cannot give this library a device buffer for the per-tensor
+// amax vector that mf_ckpt_quant_fp8 needs as scratch: a host whose device
+// memory is entirely owned by another allocator -- for instance a Go program
+// that runs manifesto graphs on the single workspace arena its planner sized
+// in advance (ir.PlanWorkspace), where no port exists for scratch -- or a
+// deployment that forbids cudaMalloc once set-up is over.  For them the amax
+// vector lives in a file-scope device array instead.
+//   * At most kNoAllocMaxTensors (4096) tensors per call (16 KB of scratch);
+//     larger calls are rejected with MF_ERR_ALLOCATOR_EXHAUSTED.
+//   * Every GPU that loads the library holds the array until the process
+//     exits, and every call on a device shares it: calls that overlap on the
+//     GPU (on streams with no ordering between them) race on it.
+//   * Each call zeroes the entries it uses before pass 1.
+//   * The first call on each device looks up the array's device address with
+//     cudaGetSymbolAddress, with that device current; make that first call
+//     before any stream capture begins.
+//   * Nothing is allocated: no cudaMalloc/cudaFree and no host heap use (the
+//     chunk table is scanned in place instead of being grouped into lists).
+namespace mf {
+namespace {
+
+constexpr int kNoAllocMaxTensors = 4096;
+__device__ __align__(256) float g_noalloc_amax[kNoAllocMaxTensors];
+constexpr int kNoAllocMaxDevices = 64;
+float* g_noalloc_amax_addr[kNoAllocMaxDevices] = {};  // device address of the array, per device
+std::mutex g_noalloc_setup_mutex;
+
+int noalloc_scratch(float** out) {
+    int dev = 0;
+    MF_CUDA_CHECK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8_noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_setup_mutex);
+    if (!g_noalloc_amax_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_amax);
+        if (err != cudaSuccess) return cuda_fail(err, "mf_ckpt_quant_fp8_noalloc: cudaGetSymbolAddress");
+        g_noalloc_amax_addr[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_amax_addr[dev];
+    return MF_OK;
+}
+
+// Pass 1 over the chunks of one source dtype, filling the argument block
+// straight from the table.  Caller holds g_group_mutex.
+template <int SRC>
+int noalloc_amax_launches(const mf_chunk_desc* chunks, int32_t n_chunks, float* d_amax, cudaStream_t s) {
+    AmaxArgs& args = g_amax_args;
+    const int grid_cap = state().sm_count * 8;
+    int32_t i = 0;
+    while (i < n_chunks) {
+        int count = 0;
+        int64_t tiles = 0;
+        for (; i < n_chunks && count < kGroupMaxChunks; ++i) {
+            const mf_chunk_desc& d = chunks[i];
+            if (d.n <= 0 || d.src_dtype != SRC) continue;
+            AmaxChunk& r = args.chunk[count++];
+            r.src = d.src;
+            r.n = d.n;
+            r.tile_begin = tiles;
+            r.tensor = d.tensor;
+            r.aligned = aligned16(d.src) ? 1 : 0;
+            tiles += (d.n + Tile<SRC>::kElems - 1) / Tile<SRC>::kElems;
+        }
+        if (count == 0) continue;
+        args.amax = d_amax;
+        args.n_chunks = count;
+        args.total_tiles = tiles;
+        const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, grid_cap));
+        group_amax_kernel<SRC><<<blocks, kThreads, 0, s>>>(args);
+        MF_LAUNCH_CHECK("mf_ckpt_quant_fp8_noalloc amax pass launch");
+    }
+    return MF_OK;
+}
+
+// Pass 2 over the chunks of one source dtype.  Caller holds g_group_mutex.
+template <int SRC>
+int noalloc_cast_launches(const mf_chunk_desc* chunks, int32_t n_chunks, const float* d_amax, float* d_scale_inv,
+                          int fp8_dtype, int compat, cudaStream_t s) {
+    StreamArgs<kGroupMaxChunks>& args = g_cast_args;
+    int32_t i = 0;
+    while (i < n_chunks) {
+        int count = 0;
+        int64_t tiles = 0;
+        for (; i < n_chunks && count < kGroupMaxChunks; ++i) {
+            const mf_chunk_desc& d = chunks[i];
+            if (d.n <= 0 || d.src_dtype != SRC) continue;
+            ChunkRec& r = args.chunk[count++];
+            r.src = d.src;
+            r.dst = d.dst;
+            r.n = d.n;
+            r.tile_begin = tiles;
+            r.tensor = d.tensor;
+            r.aligned = (aligned16(d.src) && aligned16(d.dst)) ? 1 : 0;
+            tiles += (d.n + kTileElems - 1) / kTileElems;
+        }
+        if (count == 0) continue;
+        args.amax = d_amax;
+        args.scale_inv = d_scale_inv;
+        args.status = sticky_status_ptr();
+        args.n_chunks = count;
+        args.total_tiles = tiles;
+        const cudaError_t err = (fp8_dtype == MF_DT_F8E4M3) ? cast_launch<SRC, MF_DT_F8E4M3>(args, compat, s)
+                                                            : cast_launch<SRC, MF_DT_F8E5M2>(args, compat, s);
+        if (err != cudaSuccess) return cuda_fail(err, "mf_ckpt_quant_fp8_noalloc cast pass launch");
+    }
+    return MF_OK;
+}
+
+}  // namespace
+}  // namespace mf
+
+extern "C" int mf_ckpt_quant_fp8_noalloc(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors,
+                                         float* d_scale_inv, int fp8_dtype, int compat, mf_comm comm,
+                                         mf_stream stream) {
+    MF_ENTER();
+    if (n_tensors > kNoAllocMaxTensors)
+        return fail(MF_ERR_ALLOCATOR_EXHAUSTED,
+                    "mf_ckpt_quant_fp8_noalloc: %d tensors exceed the static amax scratch of %d tensors; "
+                    "split the checkpoint or use mf_ckpt_quant_fp8 with a caller buffer",
+                    n_tensors, kNoAllocMaxTensors);
+    float* amax = nullptr;
+    int rc = noalloc_scratch(&amax);
+    if (rc) return rc;
+    rc = check_chunks("mf_ckpt_quant_fp8_noalloc", chunks, n_chunks, n_tensors, amax);
+    if (rc) return rc;
+    rc = check_fp8_mode("mf_ckpt_quant_fp8_noalloc", fp8_dtype, compat);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    MF_CUDA_CHECK(cudaMemsetAsync(amax, 0, sizeof(float) * n_tensors, s));
+    {
+        std::lock_guard<std::mutex> lock(g_group_mutex);
+        rc = noalloc_amax_launches<MF_DT_BF16>(chunks, n_chunks, amax, s);
+        if (!rc) rc = noalloc_amax_launches<MF_DT_F16>(chunks, n_chunks, amax, s);
+        if (!rc) rc = noalloc_amax_launches<MF_DT_F32>(chunks, n_chunks, amax, s);
+    }
+    if (rc) return rc;
+    if (comm) {
+        rc = comm_allreduce_max(comm, amax, n_tensors, s);
+        if (rc) return rc;
+    }
+    std::lock_guard<std::mutex> lock(g_group_mutex);
+    rc = noalloc_cast_launches<MF_DT_BF16>(chunks, n_chunks, amax, d_scale_inv, fp8_dtype, compat, s);
+    if (!rc) rc = noalloc_cast_launches<MF_DT_F16>(chunks, n_chunks, amax, d_scale_inv, fp8_dtype, compat, s);
+    if (!rc) rc = noalloc_cast_launches<MF_DT_F32>(chunks, n_chunks, amax, d_scale_inv, fp8_dtype, compat, s);
+    return rc;
+}

@@ -1,0 +1,91 @@
+"""Sharded checkpoint quantisation on 2 GPUs with the library's NCCL exchange.
+
+One process per GPU; each quantises its row range of every tensor with
+mf_ckpt_quant_fp8 and the NCCL max all-reduce of the amax vector between the
+two passes.  The shards, put back together, must equal the CPU oracle's
+single-process quantisation bit for bit.  Skipped with fewer than 2 GPUs.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _specs():
+    from manifesto_b200 import checkpoint
+    return checkpoint.llama3_8b_layout(layers=2, hidden=512, mlp=1536, heads=8, kv_heads=2, vocab=3001)
+
+
+def _tensor(i, spec):
+    from manifesto_b200 import synthetic
+    return synthetic.normal_bf16(900 + i, spec.numel, 0.0, 0.02 * (1 + i % 7))
+
+
+def _rank_main(rank: int, port: int, out_dir: str) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    from manifesto_b200 import CUDABackend, checkpoint, sync_device
+    from manifesto_b200.dtype import DType
+    from tests.gpu_util import empty, fetch, to_device
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    CUDABackend(rank)
+    store = dist.TCPStore("127.0.0.1", port, WORLD, rank == 0, timeout=datetime.timedelta(seconds=60))
+    comm = checkpoint.Communicator.from_store(store, WORLD, rank)
+    specs = _specs()
+    parts = checkpoint.partition(specs, WORLD, rank)
+    srcs, dsts, entries, sizes = [], [], [], []
+    for t, ((first, rows), s) in enumerate(zip(parts, specs)):
+        shard = _tensor(t, s)[first * s.cols:(first + rows) * s.cols]
+        srcs.append(to_device(shard))
+        dsts.append(empty(shard.size))
+        entries.append((srcs[-1].ptr, dsts[-1].ptr, shard.size, t, DType.BFLOAT16))
+        sizes.append(shard.size)
+    am = empty(4 * len(specs))
+    si = empty(4 * len(specs))
+    checkpoint.quantise(checkpoint.make_chunks(entries), len(entries), len(specs), am.ptr, si.ptr, comm=comm)
+    sync_device()
+    out = [fetch(d, n) for d, n in zip(dsts, sizes)]
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), amax=fetch(am, 4 * len(specs), np.float32),
+             scale_inv=fetch(si, 4 * len(specs), np.float32), *out)
+    comm.close()
+
+
+def test_two_gpu_nccl_quantisation(backend, ref, tmp_path):
+    from manifesto_b200 import device_count
+    if device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_rank_main, args=(r, port, str(tmp_path))) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        if p.exitcode is None:
+            p.kill()
+        assert p.exitcode == 0, f"rank exited with {p.exitcode}"
+    res = [np.load(tmp_path / f"rank{r}.npz") for r in range(WORLD)]
+    specs = _specs()
+    for t, s in enumerate(specs):
+        full = _tensor(t, s)
+        want_amax = ref.amax(full, ref.BF16)
+        for r in range(WORLD):
+            assert res[r]["amax"][t] == want_amax, (s.name, r)
+            assert res[r]["scale_inv"][t] == ref.fp8_scale_inv(want_amax, ref.E4M3)
+        got = np.concatenate([res[r][f"arr_{t}"] for r in range(WORLD)])
+        assert (got == ref.scaled_cast(full, ref.BF16, ref.E4M3, want_amax)).all(), s.name

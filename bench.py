@@ -164,14 +164,11 @@ class Dist:
             self.pg.destroy_process_group()
 
 
-def fill_normal_bf16(torch, t, seed: int, mu: float, sigma: float, chunk: int = 1 << 27) -> None:
-    """Fill a bf16 tensor with N(mu, sigma) from a seeded device generator."""
+def fill_normal_bf16(torch, t, seed: int, mu: float, sigma: float) -> None:
+    """Fill a bf16 tensor with N(mu, sigma) from a seeded device generator (one launch)."""
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
-    flat = t.view(-1)
-    for b in range(0, flat.numel(), chunk):
-        e = min(flat.numel(), b + chunk)
-        flat[b:e].copy_((torch.randn(e - b, device="cuda", generator=g) * sigma + mu).to(torch.bfloat16))
+    t.view(-1).normal_(mu, sigma, generator=g)
 
 
 def time_launches(torch, fn, reps: int, flush=None) -> list[float]:

@@ -8,7 +8,7 @@
 // build does not contract), or one fused rounding when fused_fma is set.
 // mf_scalar_broadcast replaces applyScalarBroadcast
 // (runtime/executor_math.go:195-234) plus its store encode.
-// Both stream 16-element chunks with 128-bit accesses.
+// Both work on lane-contiguous quads (4 elements per lane per access).
 // Roofline: HBM; axpy moves 3 * sizeof(dtype) bytes per element.
 #include "mf_runtime.h"
 #include "mf_vec.cuh"
@@ -25,26 +25,51 @@ __device__ __forceinline__ float axpy_op(float y, float x, float alpha) {
     else return x86_add(y, x86_mul(alpha, x));
 }
 
+// Lane-contiguous quads: lane l owns elements 4(q0 + l) .. +3, so every
+// warp access is one contiguous span; each thread keeps kUnroll quads of y
+// and of x in flight.
+constexpr int kUnroll = 4;
+
 template <int DT, int FUSED>
-__global__ void __launch_bounds__(kThreads) axpy_vec_kernel(void* __restrict__ y, const void* __restrict__ x,
+__device__ __forceinline__ void axpy_quad(void* y, const uint32_t* yw, const uint32_t* xw, int64_t q, float alpha) {
+    constexpr int B = dtype_bytes(DT);
+    float vy[4], vx[4];
+    decode4<DT>(yw, vy);
+    decode4<DT>(xw, vx);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) vy[k] = axpy_op<FUSED>(vy[k], vx[k], alpha);
+    uint32_t o[B];
+    encode4<DT>(vy, o, 0);
+    store4_stream<B>(static_cast<uint8_t*>(y) + q * 4 * B, o);
+}
+
+template <int DT, int FUSED>
+__global__ void __launch_bounds__(kThreads) axpy_vec_kernel(void* y, const void* __restrict__ x,
                                                            int64_t n, float alpha) {
     constexpr int B = dtype_bytes(DT);
-    const int64_t nchunks = n / kChunk;
+    const int64_t nq = n / 4;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nchunks; c += stride) {
-        RawChunk<B> ry, rx;
-        load_raw<B>(y, c, ry);
-        load_raw<B>(x, c, rx);
-        float vy[kChunk], vx[kChunk];
-        decode16<DT>(ry, vy);
-        decode16<DT>(rx, vx);
+    const uint8_t* yb = static_cast<const uint8_t*>(y);
+    const uint8_t* xb = static_cast<const uint8_t*>(x);
+    int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; q + (kUnroll - 1) * stride < nq; q += kUnroll * stride) {
+        uint32_t yw[kUnroll][B], xw[kUnroll][B];
 #pragma unroll
-        for (int k = 0; k < kChunk; ++k) vy[k] = axpy_op<FUSED>(vy[k], vx[k], alpha);
-        encode16<DT>(vy, ry, 0);
-        store_raw<B>(y, c, ry);
+        for (int j = 0; j < kUnroll; ++j) {
+            load4_cs<B>(yb + (q + j * stride) * 4 * B, yw[j]);
+            load4_stream<B>(xb + (q + j * stride) * 4 * B, xw[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < kUnroll; ++j) axpy_quad<DT, FUSED>(y, yw[j], xw[j], q + j * stride, alpha);
+    }
+    for (; q < nq; q += stride) {
+        uint32_t yw[B], xw[B];
+        load4_cs<B>(yb + q * 4 * B, yw);
+        load4_stream<B>(xb + q * 4 * B, xw);
+        axpy_quad<DT, FUSED>(y, yw, xw, q, alpha);
     }
     if (blockIdx.x == 0) {
-        const int64_t i = nchunks * kChunk + threadIdx.x;
+        const int64_t i = nq * 4 + threadIdx.x;
         if (i < n) {
             const float r = axpy_op<FUSED>(load_as_f32<DT>(y, i), load_as_f32<DT>(x, i), alpha);
             store_code<DT>(y, i, encode_f32<DT>(r, 0));
@@ -65,7 +90,7 @@ __global__ void __launch_bounds__(kThreads) axpy_scalar_kernel(void* __restrict_
 template <int DT>
 int launch_axpy(void* y, const void* x, int64_t n, float alpha, int fused, cudaStream_t s) {
     if (aligned16(y) && aligned16(x)) {
-        const int64_t blocks = stream_grid(n / kChunk + 1, kThreads, 8);
+        const int64_t blocks = stream_grid(n / 4 / kUnroll + 1, kThreads, 8);
         if (fused) axpy_vec_kernel<DT, 1><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(y, x, n, alpha);
         else axpy_vec_kernel<DT, 0><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(y, x, n, alpha);
     } else {
@@ -90,21 +115,39 @@ __device__ __forceinline__ float scalar_op(float v, float s) {
 template <int SRC, int DST, int OP>
 __global__ void __launch_bounds__(kThreads) scalar_vec_kernel(const void* __restrict__ src, void* __restrict__ dst,
                                                              int64_t n, float scalar) {
-    const int64_t nchunks = n / kChunk;
+    constexpr int BI = dtype_bytes(SRC), BO = dtype_bytes(DST);
+    const int64_t nq = n / 4;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nchunks; c += stride) {
-        RawChunk<dtype_bytes(SRC)> r;
-        load_raw<dtype_bytes(SRC)>(src, c, r);
-        float v[kChunk];
-        decode16<SRC>(r, v);
+    const uint8_t* sb = static_cast<const uint8_t*>(src);
+    int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; q + (kUnroll - 1) * stride < nq; q += kUnroll * stride) {
+        uint32_t w[kUnroll][BI];
 #pragma unroll
-        for (int k = 0; k < kChunk; ++k) v[k] = scalar_op<OP>(v[k], scalar);
-        RawChunk<dtype_bytes(DST)> o;
-        encode16<DST>(v, o, 0);
-        store_raw<dtype_bytes(DST)>(dst, c, o);
+        for (int j = 0; j < kUnroll; ++j) load4_cs<BI>(sb + (q + j * stride) * 4 * BI, w[j]);
+#pragma unroll
+        for (int j = 0; j < kUnroll; ++j) {
+            float v[4];
+            decode4<SRC>(w[j], v);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = scalar_op<OP>(v[k], scalar);
+            uint32_t o[BO];
+            encode4<DST>(v, o, 0);
+            store4_stream<BO>(static_cast<uint8_t*>(dst) + (q + j * stride) * 4 * BO, o);
+        }
+    }
+    for (; q < nq; q += stride) {
+        uint32_t w[BI];
+        load4_cs<BI>(sb + q * 4 * BI, w);
+        float v[4];
+        decode4<SRC>(w, v);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = scalar_op<OP>(v[k], scalar);
+        uint32_t o[BO];
+        encode4<DST>(v, o, 0);
+        store4_stream<BO>(static_cast<uint8_t*>(dst) + q * 4 * BO, o);
     }
     if (blockIdx.x == 0) {
-        const int64_t i = nchunks * kChunk + threadIdx.x;
+        const int64_t i = nq * 4 + threadIdx.x;
         if (i < n) store_code<DST>(dst, i, encode_f32<DST>(scalar_op<OP>(load_as_f32<SRC>(src, i), scalar), 0));
     }
 }
@@ -123,7 +166,7 @@ void launch_scalar_op(const void* src, void* dst, int64_t n, float scalar, cudaS
                              SRC == MF_DT_F8E5M2;
     if (kVecSrc && aligned16(src) && aligned16(dst)) {
         if constexpr (kVecSrc) {
-            const int64_t blocks = stream_grid(n / kChunk + 1, kThreads, 8);
+            const int64_t blocks = stream_grid(n / 4 / kUnroll + 1, kThreads, 8);
             scalar_vec_kernel<SRC, DST, OP><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, scalar);
         }
     } else {

@@ -182,52 +182,72 @@ __global__ void __launch_bounds__(kThreads) fused_interp_kernel(const __grid_con
 
 // -------------------------------------------- SwiGLU-style specialisation
 
-// Mul(Silu(Add(Mul(x, g), b)), y): x, y full-size BF16; g, b BF16 of length L
-// (L % 16 == 0) read at i mod L; BF16 output.
+// Mul(Silu(Add(Mul(x, g), b)), y) on one vector of 8 BF16 elements (x, g, b, y
+// as packed uint4); returns the 8 BF16 results.  With TRACK, folds |result|
+// into amax (fmaxf ignores NaN, as the reference's '>' does).
+template <bool TRACK>
+__device__ __forceinline__ uint4 swiglu8(const uint4& xv, const uint4& yv, const uint4& gv, const uint4& bv,
+                                        float& amax) {
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+    const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+    uint32_t ow[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float r[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float xf = __uint_as_float(h ? (xw[k] & 0xffff0000u) : (xw[k] << 16));
+            const float yf = __uint_as_float(h ? (yw[k] & 0xffff0000u) : (yw[k] << 16));
+            const float gf = __uint_as_float(h ? (gw[k] & 0xffff0000u) : (gw[k] << 16));
+            const float bf = __uint_as_float(h ? (bw[k] & 0xffff0000u) : (bw[k] << 16));
+            const float t = __fadd_rn(__fmul_rn(xf, gf), bf);
+            // silu(t) = t / (1 + e^-t), e^-t = 2^(-t * log2(e)) on the SFU
+            const float e = exp2f_approx(__fmul_rn(t, -1.4426950408889634f));
+            const float sl = __fmul_rn(t, rcp_approx(__fadd_rn(1.0f, e)));
+            r[h] = __fmul_rn(sl, yf);
+        }
+        ow[k] = f32x2_to_bf16x2(r[0], r[1]);
+        if constexpr (TRACK) {
+            amax = fmaxf(amax, __uint_as_float((ow[k] << 16) & 0x7fff0000u));
+            amax = fmaxf(amax, __uint_as_float(ow[k] & 0x7fff0000u));
+        }
+    }
+    return make_uint4(ow[0], ow[1], ow[2], ow[3]);
+}
+
+// x, y full-size BF16 (nvec vectors of 8); g, b BF16 of length L = 8 * row_vecs
+// read at element index mod L; BF16 output.  Lane l of a warp owns vector
+// v0 + l (a warp covers 256 contiguous elements per access); each thread
+// keeps two vectors in flight and advances the broadcast row index
+// incrementally instead of a 64-bit modulo per vector.
 template <bool AMAX>
 __global__ void __launch_bounds__(kThreads) swiglu_bf16_kernel(const uint4* __restrict__ x, const uint4* __restrict__ y,
                                                               const uint4* __restrict__ g, const uint4* __restrict__ b,
-                                                              uint4* __restrict__ out, int64_t nchunks,
-                                                              uint32_t row_chunks, float* __restrict__ d_amax) {
+                                                              uint4* __restrict__ out, int64_t nvec,
+                                                              uint32_t row_vecs, float* __restrict__ d_amax) {
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    uint32_t key = 0;
-    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nchunks; c += stride) {
-        const uint32_t rc = static_cast<uint32_t>(c % row_chunks);
-        const uint4 x0 = ld_stream(x + 2 * c), x1 = ld_stream(x + 2 * c + 1);
-        const uint4 y0 = ld_stream(y + 2 * c), y1 = ld_stream(y + 2 * c + 1);
-        const uint4 g0 = __ldg(g + 2 * rc), g1 = __ldg(g + 2 * rc + 1);
-        const uint4 b0 = __ldg(b + 2 * rc), b1 = __ldg(b + 2 * rc + 1);
-        const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-        const uint32_t yw[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
-        const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-        const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-        uint32_t ow[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            float r[2];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const float xv = __uint_as_float(h ? (xw[k] & 0xffff0000u) : (xw[k] << 16));
-                const float yv = __uint_as_float(h ? (yw[k] & 0xffff0000u) : (yw[k] << 16));
-                const float gv = __uint_as_float(h ? (gw[k] & 0xffff0000u) : (gw[k] << 16));
-                const float bv = __uint_as_float(h ? (bw[k] & 0xffff0000u) : (bw[k] << 16));
-                const float t = __fadd_rn(__fmul_rn(xv, gv), bv);
-                // silu(t) = t / (1 + e^-t); e^-t = 2^(-t*log2(e))
-                const float e = exp2f_approx(__fmul_rn(t, -1.4426950408889634f));
-                const float s = __fmul_rn(t, rcp_approx(__fadd_rn(1.0f, e)));
-                r[h] = __fmul_rn(s, yv);
-            }
-            ow[k] = f32x2_to_bf16x2(r[0], r[1]);
-            if constexpr (AMAX) {
-                const uint32_t a = ow[k] & 0x7fff7fffu;
-                key = __vmaxu2(key, a & ~__vcmpgtu2(a, 0x7f807f80u));
-            }
-        }
-        st_stream(out + 2 * c, make_uint4(ow[0], ow[1], ow[2], ow[3]));
-        st_stream(out + 2 * c + 1, make_uint4(ow[4], ow[5], ow[6], ow[7]));
+    const uint32_t step = static_cast<uint32_t>(stride % row_vecs);
+    int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    uint32_t rc = static_cast<uint32_t>(v % row_vecs);
+    float m = 0.0f;
+    for (; v + stride < nvec; v += 2 * stride) {
+        uint32_t rc2 = rc + step;
+        if (rc2 >= row_vecs) rc2 -= row_vecs;
+        const uint4 x0 = ld_stream(x + v), y0 = ld_stream(y + v);
+        const uint4 x1 = ld_stream(x + v + stride), y1 = ld_stream(y + v + stride);
+        const uint4 g0 = __ldg(g + rc), b0 = __ldg(b + rc), g1 = __ldg(g + rc2), b1 = __ldg(b + rc2);
+        st_stream(out + v, swiglu8<AMAX>(x0, y0, g0, b0, m));
+        st_stream(out + v + stride, swiglu8<AMAX>(x1, y1, g1, b1, m));
+        rc = rc2 + step;
+        if (rc >= row_vecs) rc -= row_vecs;
+    }
+    if (v < nvec) {
+        const uint4 x0 = ld_stream(x + v), y0 = ld_stream(y + v);
+        st_stream(out + v, swiglu8<AMAX>(x0, y0, __ldg(g + rc), __ldg(b + rc), m));
     }
     if constexpr (AMAX) {
-        float m = __uint_as_float(max(key & 0xffffu, key >> 16) << 16);
         __shared__ float part[kThreads / 32];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -319,7 +339,8 @@ void detect_swiglu(mf_fused_kernel_s& k) {
     if (p.in_bcast[s1] > 0 && p.in_bcast[s2] == 0) std::swap(s1, s2);
     const int sx = s1, sg = s2;
     const int64_t l = p.in_bcast[sg];
-    if (p.in_bcast[sx] != 0 || p.in_bcast[sy] != 0 || l <= 0 || l % 16 != 0 || p.in_bcast[sb] != l) return;
+    if (p.in_bcast[sx] != 0 || p.in_bcast[sy] != 0 || l <= 0 || l % 8 != 0 || p.in_bcast[sb] != l ||
+        l / 8 >= (int64_t(1) << 31)) return;
     for (int s : {sx, sg, sb, sy})
         if (p.in_dtype[s] != MF_DT_BF16) return;
     k.special = 1;
@@ -341,13 +362,13 @@ int launch_fused(const mf_fused_kernel_s& k, const void* const* inputs, void* ou
         if (!inputs[j]) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fused_launch: input %d is NULL", j);
         in.p[j] = inputs[j];
     }
-    bool special = k.special == 1 && n % 16 == 0 && aligned16(out);
+    bool special = k.special == 1 && n % 8 == 0 && aligned16(out);
     if (special)
         for (int j : {k.sx, k.sg, k.sb, k.sy}) special = special && aligned16(inputs[j]);
     if (special) {
-        const int64_t nchunks = n / 16;
-        const int64_t blocks = stream_grid(nchunks, kThreads, 8);
-        const uint32_t row_chunks = static_cast<uint32_t>(k.bcast_len / 16);
+        const int64_t nchunks = n / 8;
+        const int64_t blocks = stream_grid(nchunks / 2 + 1, kThreads, 8);
+        const uint32_t row_chunks = static_cast<uint32_t>(k.bcast_len / 8);
         if (d_amax)
             swiglu_bf16_kernel<true><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
                 static_cast<const uint4*>(inputs[k.sx]), static_cast<const uint4*>(inputs[k.sy]),

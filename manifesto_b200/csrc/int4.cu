@@ -79,6 +79,68 @@ __global__ void __launch_bounds__(kThreads) int4_dequant_vec_kernel(const uint4*
     }
 }
 
+// Word layout: a 32-bit word of q holds 8 consecutive nibbles (elements
+// 8w .. 8w+7 of a row when cols % 8 == 0).  Lane l of a warp owns word w0 + l,
+// so a warp reads 128 contiguous bytes of q and writes 32 x 8 outputs
+// contiguously (512 B of BF16) per access.  Each thread handles kWords words
+// spaced by the block size (independent loads in flight); blockIdx.y walks
+// rows, blockIdx.x covers a row in segments of kThreads * kWords words.
+// Requires cols % 8 == 0 and group % 8 == 0 (a word never straddles a group).
+constexpr int kWords = 4;
+
+template <int SDT, int ODT>
+__global__ void __launch_bounds__(kThreads) int4_dequant_words_kernel(const uint32_t* __restrict__ q,
+                                                                     const void* __restrict__ scales,
+                                                                     void* __restrict__ out, int64_t rows,
+                                                                     uint32_t words_per_row, int32_t gw_shift,
+                                                                     uint32_t group_words, int64_t ngroups) {
+    for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+        const uint32_t* qrow = q + r * words_per_row;
+        uint32_t wv[kWords];
+        float sv[kWords];
+        uint32_t widx[kWords];
+#pragma unroll
+        for (int k = 0; k < kWords; ++k) {
+            widx[k] = (blockIdx.x * kWords + k) * kThreads + threadIdx.x;
+            if (widx[k] < words_per_row) {
+                uint32_t x;
+                asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(x) : "l"(qrow + widx[k]));
+                wv[k] = x;
+                const uint32_t g = gw_shift >= 0 ? (widx[k] >> gw_shift) : (widx[k] / group_words);
+                sv[k] = load_scale<SDT>(scales, r * ngroups + g);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kWords; ++k) {
+            if (widx[k] >= words_per_row) continue;
+            const float s = sv[k];
+            float v[8];
+            if (fabsf(s) <= 3.402823466e38f) {  // finite scale: the products are finite, no NaN rule needed
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(nibble_f32(wv[k], j), s);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = x86_mul(nibble_f32(wv[k], j), s);
+            }
+            const int64_t e = (r * words_per_row + widx[k]) * 8;  // first output element
+            if constexpr (ODT == MF_DT_F32) {
+                uint4* o = reinterpret_cast<uint4*>(static_cast<float*>(out) + e);
+                st_stream(o, make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                                        __float_as_uint(v[3])));
+                st_stream(o + 1, make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]),
+                                            __float_as_uint(v[7])));
+            } else {
+                uint32_t p[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    p[j] = (ODT == MF_DT_BF16) ? f32x2_to_bf16x2(v[2 * j], v[2 * j + 1])
+                                               : f32x2_to_f16x2(v[2 * j], v[2 * j + 1]);
+                st_stream(reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + e), make_uint4(p[0], p[1], p[2], p[3]));
+            }
+        }
+    }
+}
+
 // Any shape with even cols: one element per thread-iteration.
 template <int SDT, int ODT>
 __global__ void __launch_bounds__(kThreads) int4_dequant_scalar_kernel(const uint8_t* __restrict__ q,
@@ -101,9 +163,23 @@ template <int SDT, int ODT>
 int launch(const void* q, const void* scales, void* out, int64_t rows, int64_t cols, int64_t group,
            cudaStream_t s) {
     const int64_t ngroups = (cols + group - 1) / group;
+    const bool words = (cols % 8 == 0) && (group % 8 == 0) && aligned16(q) && aligned16(out) &&
+                       (cols / 8) < (int64_t(1) << 31);
     const bool vec = (cols % kElems == 0) && (group % kElems == 0) && aligned16(q) && aligned16(out) &&
                      (cols / kElems) < (int64_t(1) << 31);
-    if (vec) {
+    if (words) {
+        const uint32_t words_per_row = static_cast<uint32_t>(cols / 8);
+        const uint32_t group_words = static_cast<uint32_t>(group / 8);
+        int32_t gw_shift = -1;
+        if ((group_words & (group_words - 1)) == 0) {
+            gw_shift = 0;
+            while ((1u << gw_shift) < group_words) ++gw_shift;
+        }
+        const uint32_t per_block = kThreads * kWords;
+        dim3 grid((words_per_row + per_block - 1) / per_block, static_cast<unsigned>(std::min<int64_t>(rows, 65535)));
+        int4_dequant_words_kernel<SDT, ODT><<<grid, kThreads, 0, s>>>(static_cast<const uint32_t*>(q), scales, out, rows,
+                                                                     words_per_row, gw_shift, group_words, ngroups);
+    } else if (vec) {
         const int64_t nchunks = rows * cols / kElems;
         const int64_t blocks = stream_grid(nchunks, kThreads, 8);
         int4_dequant_vec_kernel<SDT, ODT><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(

@@ -321,6 +321,21 @@ __device__ __forceinline__ void store4_stream(void* p, const uint32_t* w) {
     }
 }
 
+// Coherent streaming load (evict-first), for buffers the kernel also writes
+// (the in-place y of axpy): the non-coherent path requires read-only data.
+template <int Bytes>
+__device__ __forceinline__ void load4_cs(const void* p, uint32_t* w) {
+    if constexpr (Bytes == 1) {
+        asm volatile("ld.global.cs.u32 %0, [%1];" : "=r"(w[0]) : "l"(p));
+    } else if constexpr (Bytes == 2) {
+        asm volatile("ld.global.cs.v2.u32 {%0,%1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "l"(p));
+    } else {
+        asm volatile("ld.global.cs.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                     : "l"(p));
+    }
+}
+
 template <int Bytes>
 __device__ __forceinline__ void load4_stream(const void* p, uint32_t* w) {
     if constexpr (Bytes == 1) {

@@ -114,13 +114,34 @@ __global__ void __launch_bounds__(kThreads) int4_dequant_words_kernel(const uint
         for (int k = 0; k < kWords; ++k) {
             if (widx[k] >= words_per_row) continue;
             const float s = sv[k];
+            const uint32_t w = wv[k];
             float v[8];
-            if (fabsf(s) <= 3.402823466e38f) {  // finite scale: the products are finite, no NaN rule needed
+            uint32_t p[4];
+            if (fabsf(s) <= 3.402823466e38f) {
+                // Finite scale: the products are finite, so no NaN rule is needed.
+                // Low nibbles (elements 0,2,4,6) and high nibbles (1,3,5,7), each
+                // xor 8, land in the low byte of 0x4B0000nn = 2^23 + q + 8.
+                const uint32_t lo = (w & 0x0f0f0f0fu) ^ 0x08080808u;
+                const uint32_t hi = ((w >> 4) & 0x0f0f0f0fu) ^ 0x08080808u;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(nibble_f32(wv[k], j), s);
+                for (int j = 0; j < 4; ++j) {
+                    const float2 m = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7650u + j)),
+                                                 __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7650u + j)));
+                    const float2 qv = __fadd2_rn(m, make_float2(-8388616.0f, -8388616.0f));  // exact q
+                    const float2 pr = __fmul2_rn(qv, make_float2(s, s));                      // exact q * s
+                    v[2 * j] = pr.x;
+                    v[2 * j + 1] = pr.y;
+                    if constexpr (ODT == MF_DT_BF16) p[j] = f32x2_to_bf16x2_nonan(pr.x, pr.y);
+                    else if constexpr (ODT == MF_DT_F16) p[j] = f32x2_to_f16x2_nonan(pr.x, pr.y);
+                }
             } else {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = x86_mul(nibble_f32(wv[k], j), s);
+                for (int j = 0; j < 8; ++j) v[j] = x86_mul(nibble_f32(w, j), s);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if constexpr (ODT == MF_DT_BF16) p[j] = f32x2_to_bf16x2(v[2 * j], v[2 * j + 1]);
+                    else if constexpr (ODT == MF_DT_F16) p[j] = f32x2_to_f16x2(v[2 * j], v[2 * j + 1]);
+                }
             }
             const int64_t e = (r * words_per_row + widx[k]) * 8;  // first output element
             if constexpr (ODT == MF_DT_F32) {
@@ -130,11 +151,6 @@ __global__ void __launch_bounds__(kThreads) int4_dequant_words_kernel(const uint
                 st_stream(o + 1, make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]),
                                             __float_as_uint(v[7])));
             } else {
-                uint32_t p[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    p[j] = (ODT == MF_DT_BF16) ? f32x2_to_bf16x2(v[2 * j], v[2 * j + 1])
-                                               : f32x2_to_f16x2(v[2 * j], v[2 * j + 1]);
                 st_stream(reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + e), make_uint4(p[0], p[1], p[2], p[3]));
             }
         }

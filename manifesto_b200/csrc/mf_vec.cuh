@@ -129,6 +129,19 @@ __device__ __forceinline__ void decode16(const RawChunk<dtype_bytes(DT)>& r, flo
     }
 }
 
+// Packed RNE conversions for inputs known not to be NaN (the hardware and the
+// reference agree on every non-NaN value).
+__device__ __forceinline__ uint32_t f32x2_to_bf16x2_nonan(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ uint32_t f32x2_to_f16x2_nonan(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
 // float32 x2 -> packed IEEE binary16 x2 with the reference's NaN rule.
 __device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi) {
     uint32_t r;

@@ -11,7 +11,7 @@ through the C ABI (mf_ckpt_quant_fp8).
   value      params quantised per second, whole job (max-over-ranks device time)
   e2e        the same through the C ABI with host buffers: pinned host BF16 ->
              device, quantise, FP8 + scales -> host, every step
-  roofline   the dominant kernel (pass 2, group_cast_kernel) timed alone with
+  roofline   the dominant kernel (pass 2, stream_kernel<CastOp>) timed alone with
              CUDA events: 3 B/param (read BF16, write FP8) / launch time vs the
              measured HBM copy peak
   kernels    (N=1) every other benchmark config as its own kernel line: FP8->FP32
@@ -364,7 +364,7 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
     value = total_params * args.steps / (ms * 1e-3)
     job_gbs = 5.0 * total_params * args.steps / (ms * 1e-3) / 1e9
 
-    # dominant kernel alone: pass 2 (group_cast_kernel), events around each launch
+    # dominant kernel alone: pass 2 (stream_kernel<CastOp>), events around each launch
     def cast_only():
         call("mf_ckpt_cast_pass", chunks, len(entries), len(specs), amax.data_ptr(), sinv.data_ptr(), E4M3, 0,
              stream)
@@ -379,8 +379,8 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
     torch.cuda.synchronize()
     cast_bytes = 3.0 * local_params
     achieved = cast_bytes / (cast_ms * 1e-3) / 1e9
-    traffic = traffic_table().get("group_cast_kernel")
-    roofline = {"bound": "hbm", "kernel": "group_cast_kernel (pass 2: read BF16, write E4M3)",
+    traffic = traffic_table().get("ckpt_cast_pass")
+    roofline = {"bound": "hbm", "kernel": "stream_kernel<CastOp<BF16,E4M3>> (pass 2: read BF16, write E4M3)",
                 "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_src, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "frac_of_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
                 "traffic": int(traffic * local_params) if traffic else None,

@@ -172,8 +172,14 @@ def fill_normal_bf16(torch, t, seed: int, mu: float, sigma: float) -> None:
 
 
 def time_launches(torch, fn, reps: int, flush=None) -> list[float]:
-    """Per-launch device times (ms) with CUDA events on torch's current stream."""
-    out = []
+    """Per-launch device times (ms) with CUDA events on torch's current stream.
+
+    All (flush, start, launch, end) sets are queued before one synchronisation,
+    so the device never idles waiting for the host between an event and its
+    launch (the host-side call overhead stays outside the measured interval).
+    """
+    torch.cuda.synchronize()
+    pairs = []
     for _ in range(reps):
         if flush is not None:
             flush()
@@ -181,9 +187,9 @@ def time_launches(torch, fn, reps: int, flush=None) -> list[float]:
         s.record()
         fn()
         e.record()
-        e.synchronize()
-        out.append(s.elapsed_time(e))
-    return out
+        pairs.append((s, e))
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in pairs]
 
 
 def kernel_line(name: str, alg_bytes: float, times_ms: list[float], peak: float, elems: int) -> dict:

@@ -206,14 +206,14 @@ KERNEL_CONFIGS = ("c1", "c2", "c3", "c4")
 def bench_kernels(torch, stream_handle: int, peak: float, which=KERNEL_CONFIGS, reps: int = 20) -> dict:
     """Configs 1-4 on one GPU, each kernel timed alone with L2 flushed before every launch."""
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
-    flush_sum = torch.empty((), dtype=torch.int64, device="cuda")
+    flush_words = flush_buf.view(torch.int64)
 
     def flush():
         # Write a buffer 4x the L2, then read it back: the read evicts the
         # write's dirty lines, so the timed kernel starts with a cold L2 that
         # holds none of its inputs and no write-backs owed by someone else.
         flush_buf.fill_(1)
-        torch.sum(flush_buf, dtype=torch.int64, out=flush_sum)
+        torch.amax(flush_words)
     out = {}
     for name in which:
         out.update({"c1": _kernel_c1, "c2": _kernel_c2, "c3": _kernel_c3, "c4": _kernel_c4}[name](

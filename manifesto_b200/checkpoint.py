@@ -122,3 +122,75 @@ def quantise(chunks: ctypes.Array, n_chunks: int, n_tensors: int, d_amax: int, d
     """mf_ckpt_quant_fp8: pass 1, optional all-reduce, pass 2 (no host sync)."""
     call("mf_ckpt_quant_fp8", chunks, int(n_chunks), int(n_tensors), int(d_amax), d_scale_inv, int(fp8_dtype),
          int(compat), comm.handle if comm is not None else None, stream_handle(stream))
+
+
+class StreamedQuantiser:
+    """Quantise checkpoints that live in (pinned) host memory, one after another.
+
+    A checkpoint shard is uploaded, quantised and downloaded in a pipeline of
+    three CUDA streams -- upload, compute, download -- over two device slots,
+    so the FP8 download of checkpoint i runs on the PCIe link while the BF16
+    upload of checkpoint i+1 runs in the other direction, and the kernels run
+    between them.  ``submit`` returns as soon as the work is queued.
+
+    sizes[t] is this rank's element count of tensor t (its row range); the
+    host buffers hold the shards back to back in tensor order: BF16 source
+    (2 bytes per element), FP8 destination (1 byte per element) and the
+    float32 scale_inv vector.
+    """
+
+    def __init__(self, sizes: Sequence[int], fp8_dtype: DType = DType.FLOAT8_E4M3, compat: int = 0,
+                 comm: Communicator | None = None, src_dtype: DType = DType.BFLOAT16):
+        from .backend import DeviceBuffer, Event, Stream
+        self.sizes = [int(s) for s in sizes]
+        self.n_tensors = len(self.sizes)
+        self.total = sum(self.sizes)
+        self.esize = 2 if src_dtype in (DType.BFLOAT16, DType.FLOAT16) else 4
+        self.src_dtype, self.fp8_dtype, self.compat, self.comm = src_dtype, fp8_dtype, compat, comm
+        self.up, self.compute, self.down = Stream(), Stream(), Stream()
+        self.slots = []
+        for _ in range(2):
+            src = DeviceBuffer(max(1, self.esize * self.total))
+            dst = DeviceBuffer(max(1, self.total))
+            amax = DeviceBuffer(4 * self.n_tensors)
+            sinv = DeviceBuffer(4 * self.n_tensors)
+            entries, off = [], 0
+            for t, n in enumerate(self.sizes):
+                entries.append((src.ptr + self.esize * off, dst.ptr + off, n, t, src_dtype))
+                off += n
+            self.slots.append({"src": src, "dst": dst, "amax": amax, "sinv": sinv,
+                               "chunks": make_chunks(entries), "uploaded": Event(), "computed": Event(),
+                               "downloaded": Event(), "used": False})
+        self.count = 0
+
+    def submit(self, host_src: int, host_dst: int, host_scale_inv: int) -> None:
+        """Queue one checkpoint: host_src -> device -> quantise -> host_dst, host_scale_inv."""
+        s = self.slots[self.count % 2]
+        if s["used"]:
+            self.up.wait(s["downloaded"])  # the slot's previous results have left the device
+        call("mf_memcpy_h2d_async", s["src"].ptr, int(host_src), self.esize * self.total, self.up.handle)
+        s["uploaded"].record(self.up)
+        self.compute.wait(s["uploaded"])
+        quantise(s["chunks"], self.n_tensors, self.n_tensors, s["amax"].ptr, s["sinv"].ptr, self.fp8_dtype,
+                 self.compat, self.comm, self.compute)
+        s["computed"].record(self.compute)
+        self.down.wait(s["computed"])
+        call("mf_memcpy_d2h_async", int(host_dst), s["dst"].ptr, self.total, self.down.handle)
+        call("mf_memcpy_d2h_async", int(host_scale_inv), s["sinv"].ptr, 4 * self.n_tensors, self.down.handle)
+        s["downloaded"].record(self.down)
+        s["used"] = True
+        self.count += 1
+
+    def synchronize(self) -> None:
+        for st in (self.up, self.compute, self.down):
+            st.sync()
+
+    def close(self) -> None:
+        self.synchronize()
+        for s in self.slots:
+            for k in ("src", "dst", "amax", "sinv"):
+                s[k].free()
+            for k in ("uploaded", "computed", "downloaded"):
+                s[k].close()
+        for st in (self.up, self.compute, self.down):
+            st.close()

@@ -311,6 +311,34 @@ def test_ckpt_many_chunks_and_ragged(backend, ref):
         b.free()
 
 
+def test_streamed_quantiser_host_checkpoints(backend, ref):
+    """Three host-resident checkpoints through the upload/compute/download pipeline (two slots)."""
+    from manifesto_b200 import PinnedBuffer
+    specs = small_layout()
+    sizes = [s.numel for s in specs]
+    total = sum(sizes)
+    q = checkpoint.StreamedQuantiser(sizes)
+    ins, outs, sis, hosts = [], [], [], []
+    for k in range(3):
+        host = [synthetic.normal_bf16(4000 + 100 * k + i, n, 0.0, 0.02 * (k + 1)) for i, n in enumerate(sizes)]
+        hs = PinnedBuffer(2 * total)
+        hs.array[:] = np.concatenate(host).view(np.uint8)
+        hd, hsi = PinnedBuffer(total), PinnedBuffer(4 * len(sizes))
+        q.submit(hs.ptr, hd.ptr, hsi.ptr)
+        ins.append(hs), outs.append(hd), sis.append(hsi), hosts.append(host)
+    q.synchronize()
+    for k in range(3):
+        off = 0
+        for t, n in enumerate(sizes):
+            a = ref.amax(hosts[k][t], BF16)
+            assert float(sis[k].array.view(np.float32)[t]) == ref.fp8_scale_inv(a, E4M3)
+            bits_equal(outs[k].array[off:off + n], ref.scaled_cast(hosts[k][t], BF16, E4M3, a))
+            off += n
+    q.close()
+    for b in ins + outs + sis:
+        b.free()
+
+
 def test_ckpt_rejects(backend):
     arr = checkpoint.make_chunks([(1, 1, 10, 5, DType.BFLOAT16)])
     assert lib().mf_ckpt_quant_fp8(arr, 1, 2, 1, None, E4M3, 0, None, None) == -1  # tensor 5 of 2

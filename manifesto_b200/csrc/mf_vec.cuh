@@ -200,15 +200,17 @@ __device__ __forceinline__ uint32_t bytes_from_bit7(uint32_t hi) { return hi | (
 // a band value is fixed with a second hardware conversion and byte masks;
 // only a NaN or a value of exactly 2^-10 (the hardware rounds that tie to 0,
 // the reference to 1) falls back to the scalar routine.
-static __device__ __noinline__ uint32_t e4m3_ref_low(uint32_t res, uint32_t c, float v0, float v1, float v2,
-                                                     float v3) {
+static __device__ __noinline__ uint32_t e4m3_ref_scalar4(float v0, float v1, float v2, float v3) {
+    return f32bits_to_e4m3_ref(__float_as_uint(v0)) | (f32bits_to_e4m3_ref(__float_as_uint(v1)) << 8) |
+           (f32bits_to_e4m3_ref(__float_as_uint(v2)) << 16) | (f32bits_to_e4m3_ref(__float_as_uint(v3)) << 24);
+}
+
+__device__ __forceinline__ uint32_t e4m3_ref_low(uint32_t res, uint32_t c, float v0, float v1, float v2, float v3) {
     const uint32_t c7 = c & 0x7f7f7f7fu;
     const bool nan = ((c7 + 0x01010101u) & 0x80808080u) != 0;
     const bool tie = (fabsf(v0) == 0.0009765625f) | (fabsf(v1) == 0.0009765625f) | (fabsf(v2) == 0.0009765625f) |
                      (fabsf(v3) == 0.0009765625f);
-    if (nan | tie)
-        return f32bits_to_e4m3_ref(__float_as_uint(v0)) | (f32bits_to_e4m3_ref(__float_as_uint(v1)) << 8) |
-               (f32bits_to_e4m3_ref(__float_as_uint(v2)) << 16) | (f32bits_to_e4m3_ref(__float_as_uint(v3)) << 24);
+    if (nan | tie) return e4m3_ref_scalar4(v0, v1, v2, v3);
     // band lanes: hardware code in [1, 8] (y has a zero byte exactly there)
     const uint32_t y = ((c7 + 0x77777777u) ^ 0x78787878u) & 0xf8f8f8f8u;
     const uint32_t band = bytes_from_bit7(~(((y & 0x7f7f7f7fu) + 0x7f7f7f7fu) | y) & 0x80808080u);

@@ -237,7 +237,7 @@ def _kernel_c1(torch, stream_handle, peak, flush, reps) -> dict:
     dst = torch.empty(n, dtype=torch.float32, device="cuda")
     f = lambda: call("mf_convert", 5, 2, src.data_ptr(), dst.data_ptr(), n, 0, stream_handle)
     _warm(f)
-    return {"c1_fp8e4m3_to_f32": kernel_line("convert_vec_kernel<E4M3,F32>", 5 * n,
+    return {"c1_fp8e4m3_to_f32": kernel_line("stream_kernel<ConvertOp<E4M3,F32>>", 5 * n,
                                              time_launches(torch, f, reps, flush), peak, n)}
 
 
@@ -252,7 +252,7 @@ def _kernel_c2(torch, stream_handle, peak, flush, reps) -> dict:
                      stream_handle)
     _warm(f)
     b = rows * cols // 2 + sc.numel() * 2 + rows * cols * 2
-    return {"c2_int4_to_bf16": kernel_line("int4_dequant_vec_kernel<BF16,BF16>", b,
+    return {"c2_int4_to_bf16": kernel_line("int4_dequant_words_kernel<BF16,BF16>", b,
                                            time_launches(torch, f, reps, flush), peak, rows * cols)}
 
 
@@ -297,14 +297,14 @@ def _kernel_c4(torch, stream_handle, peak, flush, reps) -> dict:
     ptrs = [x.data_ptr(), g.data_ptr(), be.data_ptr(), y.data_ptr()]
     f = lambda: k.run_fp8(ptrs, pre.data_ptr(), qo.data_ptr(), n, am.data_ptr(), si.data_ptr(), stream=stream_handle)
     _warm(f)
-    out["c4_fused_swiglu_fp8"] = kernel_line("swiglu_bf16_kernel + scaled_cast_vec_kernel", 9 * n,
+    out["c4_fused_swiglu_fp8"] = kernel_line("swiglu_rows_kernel + stream_kernel<CastOp<BF16,E4M3>>", 9 * n,
                                              time_launches(torch, f, max(5, reps // 2), flush), peak, n)
     f1 = lambda: k.run(ptrs, pre.data_ptr(), n, amax=am.data_ptr(), stream=stream_handle)
-    out["c4_pass1_swiglu"] = kernel_line("swiglu_bf16_kernel<amax>", 6 * n,
+    out["c4_pass1_swiglu"] = kernel_line("swiglu_rows_kernel<amax>", 6 * n,
                                          time_launches(torch, f1, max(5, reps // 2), flush), peak, n)
     f2 = lambda: call("mf_fp8_scaled_cast", pre.data_ptr(), 4, qo.data_ptr(), 5, am.data_ptr(), si.data_ptr(), n, 0,
                       stream_handle)
-    out["c4_pass2_cast"] = kernel_line("scaled_cast_vec_kernel<BF16,E4M3>", 3 * n,
+    out["c4_pass2_cast"] = kernel_line("stream_kernel<CastOp<BF16,E4M3>>", 3 * n,
                                        time_launches(torch, f2, max(5, reps // 2), flush), peak, n)
     out["c4_fused_swiglu_fp8"]["single_pass_lower_bound_bytes"] = 5 * n
     k.close()

@@ -14,10 +14,12 @@
 //   * a hand-specialised body for Mul(Silu(Add(Mul(x, g), b)), y) with BF16
 //     inputs/output and g, b broadcast along the last dimension -- the SwiGLU-style
 //     chain manifesto's fuser builds (optimizer/optimizer_test.go SwiGLU case).  It
-//     streams 16-element chunks with 128-bit accesses and evaluates SiLU in float32
-//     (ex2.approx + fast reciprocal); the result is within 1 BF16 ulp of the
-//     float64 reference formula, which is the tolerance this chain is held to.
-//     With amax requested it folds max|out| on the BF16 bit patterns (__vmaxu2).
+//     streams 8-element vectors with 128-bit accesses; each thread keeps one row
+//     position of g and b decoded in registers (the grid holds a multiple of the
+//     row length in vectors), and SiLU runs in float32 on the SFU (ex2 + reciprocal)
+//     except where t < -80, which takes the interpreter's float64 formula; the
+//     result is within 1 BF16 ulp of the reference, the tolerance this chain is
+//     held to.  With amax requested it folds max|out| on the packed BF16 results.
 #include <algorithm>
 #include <cstring>
 #include <new>
@@ -182,73 +184,109 @@ __global__ void __launch_bounds__(kThreads) fused_interp_kernel(const __grid_con
 
 // -------------------------------------------- SwiGLU-style specialisation
 
-// Mul(Silu(Add(Mul(x, g), b)), y) on one vector of 8 BF16 elements (x, g, b, y
-// as packed uint4); returns the 8 BF16 results.  With TRACK, folds |result|
-// into amax (fmaxf ignores NaN, as the reference's '>' does).
+// Below this t the fast SiLU hands over to the float64 formula: e^-t passes
+// 2^115 at t = -80, well before 1/(1 + e^-t) turns subnormal (t = -87.3) or
+// exp2 overflows (t = -88.7).  As an unsigned bit pattern, t < -80 (and a
+// negative NaN) is exactly "bits > kSiluFastFloorBits".
+constexpr uint32_t kSiluFastFloorBits = 0xC2A00000u;  // -80.0f
+
+__device__ __forceinline__ float2 bf16x2_to_f32x2(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// SFU 2^x and 1/x with flush-to-zero.  On the fast path the argument of 2^x
+// is below 115.5 and a subnormal 2^x only ever meets "1 +"; 1 + e^-t lies in
+// [1, 2^116), so its reciprocal is a normal float: flushing changes nothing.
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_ftz(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// The interpreter's float64 SiLU, out of line: the hot loop keeps its registers.
+static __device__ __noinline__ float silu_f64(float t) { return apply_unary(NODE_SILU, t); }
+
+// Running max(|acc|, |w|) per BF16 half (maxNum: a NaN half never wins).  The
+// result's sign bits are the XOR of the inputs' signs and mean nothing; the
+// caller clears them at the end.
+__device__ __forceinline__ uint32_t bf16x2_absmax(uint32_t acc, uint32_t w) {
+    uint32_t r;
+    asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(w));
+    return r;
+}
+
+// BF16 pack of a float pair, round to nearest even.  A NaN comes out as the
+// hardware's canonical NaN: the payload of a NaN created inside the chain is
+// platform-defined (the reference's amd64 arithmetic and the GPU differ) and
+// outputs are compared with NaN as a class.
+__device__ __forceinline__ uint32_t pack_bf16x2(float2 r) {
+    uint32_t o;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(o) : "f"(r.y), "f"(r.x));
+    return o;
+}
+
+// Mul(Silu(Add(Mul(x, g), b)), y) on one vector of 8 BF16 elements: x, y packed
+// in uint4, g and b already decoded (gf[k], bf[k] = elements 2k, 2k+1).  Every
+// step rounds like the reference's float32 nodes (x*g rounded, then + b
+// rounded); SiLU runs on the SFU within a few float32 ulps, or -- for a vector
+// holding any t < -80 -- through the interpreter's float64 formula.  With TRACK
+// the |result| halves are folded into amax2.
 template <bool TRACK>
-__device__ __forceinline__ uint4 swiglu8(const uint4& xv, const uint4& yv, const uint4& gv, const uint4& bv,
-                                        float& amax) {
+__device__ __forceinline__ uint4 swiglu8(const uint4& xv, const uint4& yv, const float2 (&gf)[4],
+                                        const float2 (&bf)[4], uint32_t& amax2) {
     const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
     const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
-    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-    const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+    float2 t[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) t[k] = __fadd2_rn(__fmul2_rn(bf16x2_to_f32x2(xw[k]), gf[k]), bf[k]);
+    const uint32_t hi =
+        max(__vimax3_u32(__float_as_uint(t[0].x), __float_as_uint(t[0].y), __float_as_uint(t[1].x)),
+            __vimax3_u32(__float_as_uint(t[1].y), __float_as_uint(t[2].x),
+                         __vimax3_u32(__float_as_uint(t[2].y), __float_as_uint(t[3].x), __float_as_uint(t[3].y))));
+    float2 sl[4];
+    if (hi > kSiluFastFloorBits) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) sl[k] = make_float2(silu_f64(t[k].x), silu_f64(t[k].y));
+    } else {
+        // silu(t) = t / (1 + e^-t), e^-t = 2^(-t * log2(e))
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 a = __fmul2_rn(t[k], make_float2(-1.4426950408889634f, -1.4426950408889634f));
+            const float2 d = __fadd2_rn(make_float2(ex2_ftz(a.x), ex2_ftz(a.y)), make_float2(1.0f, 1.0f));
+            sl[k] = __fmul2_rn(t[k], make_float2(rcp_ftz(d.x), rcp_ftz(d.y)));
+        }
+    }
     uint32_t ow[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        float r[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const float xf = __uint_as_float(h ? (xw[k] & 0xffff0000u) : (xw[k] << 16));
-            const float yf = __uint_as_float(h ? (yw[k] & 0xffff0000u) : (yw[k] << 16));
-            const float gf = __uint_as_float(h ? (gw[k] & 0xffff0000u) : (gw[k] << 16));
-            const float bf = __uint_as_float(h ? (bw[k] & 0xffff0000u) : (bw[k] << 16));
-            const float t = __fadd_rn(__fmul_rn(xf, gf), bf);
-            // silu(t) = t / (1 + e^-t), e^-t = 2^(-t * log2(e)) on the SFU
-            const float e = exp2f_approx(__fmul_rn(t, -1.4426950408889634f));
-            const float sl = __fmul_rn(t, rcp_approx(__fadd_rn(1.0f, e)));
-            r[h] = __fmul_rn(sl, yf);
-        }
-        ow[k] = f32x2_to_bf16x2(r[0], r[1]);
-        if constexpr (TRACK) {
-            amax = fmaxf(amax, __uint_as_float((ow[k] << 16) & 0x7fff0000u));
-            amax = fmaxf(amax, __uint_as_float(ow[k] & 0x7fff0000u));
-        }
+        ow[k] = pack_bf16x2(__fmul2_rn(sl[k], bf16x2_to_f32x2(yw[k])));
+        if constexpr (TRACK) amax2 = bf16x2_absmax(amax2, ow[k]);
     }
     return make_uint4(ow[0], ow[1], ow[2], ow[3]);
 }
 
-// x, y full-size BF16 (nvec vectors of 8); g, b BF16 of length L = 8 * row_vecs
-// read at element index mod L; BF16 output.  Lane l of a warp owns vector
-// v0 + l (a warp covers 256 contiguous elements per access); each thread
-// keeps two vectors in flight and advances the broadcast row index
-// incrementally instead of a 64-bit modulo per vector.
+__device__ __forceinline__ void decode_row(const uint4& gv, const uint4& bv, float2 (&gf)[4], float2 (&bf)[4]) {
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+    const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        gf[k] = bf16x2_to_f32x2(gw[k]);
+        bf[k] = bf16x2_to_f32x2(bw[k]);
+    }
+}
+
+// Block-wide max of the packed amax and one atomicMax per block.
 template <bool AMAX>
-__global__ void __launch_bounds__(kThreads) swiglu_bf16_kernel(const uint4* __restrict__ x, const uint4* __restrict__ y,
-                                                              const uint4* __restrict__ g, const uint4* __restrict__ b,
-                                                              uint4* __restrict__ out, int64_t nvec,
-                                                              uint32_t row_vecs, float* __restrict__ d_amax) {
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    const uint32_t step = static_cast<uint32_t>(stride % row_vecs);
-    int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    uint32_t rc = static_cast<uint32_t>(v % row_vecs);
-    float m = 0.0f;
-    for (; v + stride < nvec; v += 2 * stride) {
-        uint32_t rc2 = rc + step;
-        if (rc2 >= row_vecs) rc2 -= row_vecs;
-        const uint4 x0 = ld_stream(x + v), y0 = ld_stream(y + v);
-        const uint4 x1 = ld_stream(x + v + stride), y1 = ld_stream(y + v + stride);
-        const uint4 g0 = __ldg(g + rc), b0 = __ldg(b + rc), g1 = __ldg(g + rc2), b1 = __ldg(b + rc2);
-        st_stream(out + v, swiglu8<AMAX>(x0, y0, g0, b0, m));
-        st_stream(out + v + stride, swiglu8<AMAX>(x1, y1, g1, b1, m));
-        rc = rc2 + step;
-        if (rc >= row_vecs) rc -= row_vecs;
-    }
-    if (v < nvec) {
-        const uint4 x0 = ld_stream(x + v), y0 = ld_stream(y + v);
-        st_stream(out + v, swiglu8<AMAX>(x0, y0, __ldg(g + rc), __ldg(b + rc), m));
-    }
+__device__ __forceinline__ void swiglu_amax_flush(uint32_t m2, float* d_amax) {
     if constexpr (AMAX) {
         __shared__ float part[kThreads / 32];
+        m2 &= 0x7fff7fffu;
+        float m = fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xffff0000u));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
@@ -260,6 +298,65 @@ __global__ void __launch_bounds__(kThreads) swiglu_bf16_kernel(const uint4* __re
             if (threadIdx.x == 0 && m > 0.0f) atomicMax(reinterpret_cast<unsigned int*>(d_amax), __float_as_uint(m));
         }
     }
+}
+
+// x, y full-size BF16 (nvec vectors of 8); g, b BF16 of length L = 8 * row_vecs
+// read at element index mod L; BF16 output.  The launch holds a multiple of
+// row_vecs threads, so thread i only ever meets row vector i mod row_vecs: it
+// decodes its slice of g and b once and keeps it in registers.  Lane l of a
+// warp owns vector v0 + l (a warp covers 256 contiguous elements per access);
+// each thread keeps two vectors in flight.
+template <bool AMAX>
+__global__ void __launch_bounds__(kThreads, 4) swiglu_rows_kernel(const uint4* __restrict__ x, const uint4* __restrict__ y,
+                                                              const uint4* __restrict__ g, const uint4* __restrict__ b,
+                                                              uint4* __restrict__ out, int64_t nvec,
+                                                              uint32_t row_vecs, float* __restrict__ d_amax) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint32_t rc = static_cast<uint32_t>(v % row_vecs);
+    float2 gf[4], bf[4];
+    decode_row(__ldg(g + rc), __ldg(b + rc), gf, bf);
+    uint32_t m2 = 0u;
+    for (; v + stride < nvec; v += 2 * stride) {
+        const uint4 x0 = ld_stream(x + v), y0 = ld_stream(y + v);
+        const uint4 x1 = ld_stream(x + v + stride), y1 = ld_stream(y + v + stride);
+        st_stream(out + v, swiglu8<AMAX>(x0, y0, gf, bf, m2));
+        st_stream(out + v + stride, swiglu8<AMAX>(x1, y1, gf, bf, m2));
+    }
+    if (v < nvec) st_stream(out + v, swiglu8<AMAX>(ld_stream(x + v), ld_stream(y + v), gf, bf, m2));
+    swiglu_amax_flush<AMAX>(m2, d_amax);
+}
+
+// The same chain for any row length: the row index advances incrementally
+// (a grid-stride step mod row_vecs) and g, b are decoded per vector.
+template <bool AMAX>
+__global__ void __launch_bounds__(kThreads) swiglu_bf16_kernel(const uint4* __restrict__ x, const uint4* __restrict__ y,
+                                                              const uint4* __restrict__ g, const uint4* __restrict__ b,
+                                                              uint4* __restrict__ out, int64_t nvec,
+                                                              uint32_t row_vecs, float* __restrict__ d_amax) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const uint32_t step = static_cast<uint32_t>(stride % row_vecs);
+    int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    uint32_t rc = static_cast<uint32_t>(v % row_vecs);
+    uint32_t m2 = 0u;
+    for (; v < nvec; v += stride) {
+        float2 gf[4], bf[4];
+        decode_row(__ldg(g + rc), __ldg(b + rc), gf, bf);
+        st_stream(out + v, swiglu8<AMAX>(ld_stream(x + v), ld_stream(y + v), gf, bf, m2));
+        rc += step;
+        if (rc >= row_vecs) rc -= row_vecs;
+    }
+    swiglu_amax_flush<AMAX>(m2, d_amax);
+}
+
+// Grid for the row-stationary kernel: a multiple of row_vecs threads near
+// `target` blocks, or 0 when no such grid fits.
+int64_t swiglu_rows_grid(int64_t row_vecs, int64_t target) {
+    int64_t gcd = row_vecs, t = kThreads;
+    while (t) { const int64_t r = gcd % t; gcd = t; t = r; }
+    const int64_t unit = row_vecs / gcd;  // blocks per grid unit
+    if (unit > 4 * target) return 0;
+    return std::max<int64_t>(1, (target + unit / 2) / unit) * unit;
 }
 
 }  // namespace
@@ -366,19 +463,30 @@ int launch_fused(const mf_fused_kernel_s& k, const void* const* inputs, void* ou
     if (special)
         for (int j : {k.sx, k.sg, k.sb, k.sy}) special = special && aligned16(inputs[j]);
     if (special) {
-        const int64_t nchunks = n / 8;
-        const int64_t blocks = stream_grid(nchunks / 2 + 1, kThreads, 8);
-        const uint32_t row_chunks = static_cast<uint32_t>(k.bcast_len / 8);
-        if (d_amax)
-            swiglu_bf16_kernel<true><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
-                static_cast<const uint4*>(inputs[k.sx]), static_cast<const uint4*>(inputs[k.sy]),
-                static_cast<const uint4*>(inputs[k.sg]), static_cast<const uint4*>(inputs[k.sb]),
-                static_cast<uint4*>(out), nchunks, row_chunks, d_amax);
-        else
-            swiglu_bf16_kernel<false><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
-                static_cast<const uint4*>(inputs[k.sx]), static_cast<const uint4*>(inputs[k.sy]),
-                static_cast<const uint4*>(inputs[k.sg]), static_cast<const uint4*>(inputs[k.sb]),
-                static_cast<uint4*>(out), nchunks, row_chunks, nullptr);
+        const int64_t nvec = n / 8;
+        const uint32_t row_vecs = static_cast<uint32_t>(k.bcast_len / 8);
+        const auto* x = static_cast<const uint4*>(inputs[k.sx]);
+        const auto* y = static_cast<const uint4*>(inputs[k.sy]);
+        const auto* g = static_cast<const uint4*>(inputs[k.sg]);
+        const auto* b = static_cast<const uint4*>(inputs[k.sb]);
+        auto* o = static_cast<uint4*>(out);
+        // 4 resident blocks of 256 per SM; no more blocks than vector pairs
+        const int64_t target = std::min<int64_t>(static_cast<int64_t>(state().sm_count) * 4,
+                                                 (nvec / 2 + kThreads - 1) / kThreads);
+        const int64_t rows_grid = swiglu_rows_grid(row_vecs, std::max<int64_t>(target, 1));
+        if (rows_grid > 0 && rows_grid <= 0x7fffffff) {
+            const unsigned grid = static_cast<unsigned>(rows_grid);
+            if (d_amax)
+                swiglu_rows_kernel<true><<<grid, kThreads, 0, s>>>(x, y, g, b, o, nvec, row_vecs, d_amax);
+            else
+                swiglu_rows_kernel<false><<<grid, kThreads, 0, s>>>(x, y, g, b, o, nvec, row_vecs, nullptr);
+        } else {
+            const unsigned grid = static_cast<unsigned>(stream_grid(nvec, kThreads, 8));
+            if (d_amax)
+                swiglu_bf16_kernel<true><<<grid, kThreads, 0, s>>>(x, y, g, b, o, nvec, row_vecs, d_amax);
+            else
+                swiglu_bf16_kernel<false><<<grid, kThreads, 0, s>>>(x, y, g, b, o, nvec, row_vecs, nullptr);
+        }
     } else {
         switch (k.prog.out_dtype) {
         case MF_DT_BF16: launch_interp<MF_DT_BF16>(k, in, out, n, d_amax, s); break;

@@ -157,6 +157,36 @@ def test_swiglu_specialised_within_1ulp(backend, ref):
     assert amax == float(np.abs((got.astype(np.uint32) << 16).view(np.float32)).max())
 
 
+def test_swiglu_specialised_extreme_inputs(backend, ref):
+    """t = x*g + b swept through the range where e^-t leaves float32 (t < -88.7) and
+    1/(1 + e^-t) turns subnormal, plus Inf, NaN, zeros and subnormal inputs: the fast
+    SiLU's float64 hand-over keeps every output within 1 BF16 ulp of the reference."""
+    hidden = 4096
+    n = hidden * 64
+    rng = np.random.default_rng(2024)
+    xf = rng.uniform(-140.0, 140.0, n).astype(np.float32)
+    xf[: 4096] = np.linspace(-130.0, -70.0, 4096, dtype=np.float32)
+    specials = np.array([np.inf, -np.inf, np.nan, 0.0, -0.0, 1e-40, -1e-40, 3e38, -3e38], np.float32)
+    xf[5000:5000 + specials.size] = specials
+    yf = rng.standard_normal(n).astype(np.float32)
+    yf[6000:6000 + specials.size] = specials
+    yf[: 4096 : 7] = 3e38  # huge y on tiny silu outputs
+    x, y = synthetic.f32_to_bf16_bits(xf), synthetic.f32_to_bf16_bits(yf)
+    g = synthetic.normal_bf16(11, hidden, 1.0, 0.1)
+    b = synthetic.normal_bf16(12, hidden, 0.0, 0.1)
+    g[7] = 0x7F80  # +Inf
+    b[9] = 0x7FC0  # NaN
+    f, k = swiglu_kernel(hidden)
+    assert k.specialised()
+    got, amax = run_fused(k, [x, g, b, y], n, BF16, amax=True)
+    want = ref.fused_eval(fusion.node_table(f.root), [x, g, b, y], [BF16] * 4, [0, hidden, hidden, 0], BF16, n,
+                          threads=host_threads())
+    d = ulp_diff_16(got, want)
+    assert d.max() <= 1, np.nonzero(d > 1)[0][:8]
+    mags = (got.astype(np.uint32) << 16).view(np.float32)
+    assert amax == float(np.nanmax(np.abs(mags)))
+
+
 def test_swiglu_commuted_forms_specialise(backend):
     x, g, b, y = (fusion.input_node(i, DType.BFLOAT16) for i in range(4))
     root = fusion.binary(N.MUL, y, fusion.unary(N.SILU, fusion.binary(N.ADD, b, fusion.binary(N.MUL, g, x))))

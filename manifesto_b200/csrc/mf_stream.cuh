@@ -31,6 +31,7 @@
 namespace mf {
 
 constexpr int kStreamThreads = 256;
+constexpr int kConsumerWarps = kStreamThreads / 32;
 constexpr int64_t kTileElems = 8192;            // elements per tile
 constexpr int kStreamSmemBudget = 64 * 1024;    // staging bytes per CTA (3 CTAs per SM)
 constexpr uint32_t kMbarSpinLimit = 1u << 24;   // polls of try_wait before giving up
@@ -122,25 +123,104 @@ __device__ __forceinline__ void load_raw_smem(const uint8_t* tile, int c, RawChu
     }
 }
 
+// ------------------------------------------------------ deferred fix-ups
+//
+// The reference's FP8 encoders differ from the hardware conversion on a few
+// value classes (E4M3: NaN, the subnormal band, 2^-10 exactly; E5M2: NaN, the
+// subnormal band, overflow).  On data with many values near zero (activations)
+// a quarter to half of all warp-wide quad steps hold at least one such value,
+// and fixing it inline makes the whole warp run the fix-up.  Instead each warp
+// parks the quads that need it in a 32-slot shared-memory queue (ballot +
+// prefix count; the lane skips its store) and encodes the parked quads
+// together at the end of the tile, one quad per lane.
+constexpr int kFixSlots = 32;
+
+struct FixQueue {
+    float4* v;   // this warp's slots: a parked quad's four values
+    int64_t* e;  // and its first element index within the chunk
+    uint32_t n;  // filled slots (warp-uniform)
+};
+
+template <class Op>
+__device__ __forceinline__ void fix_drain(FixQueue& fq, const ChunkRec& ch) {
+    __syncwarp();
+    const uint32_t lane = threadIdx.x & 31;
+    if (lane < fq.n) Op::fix(ch, fq.v[lane], fq.e[lane]);
+    __syncwarp();
+    fq.n = 0;
+}
+
+// Warp-collective (all 32 lanes): park this lane's quad when `fix` is set.
+template <class Op>
+__device__ __forceinline__ void fix_push(FixQueue& fq, bool fix, const float (&v)[4], int64_t e, const ChunkRec& ch) {
+    const uint32_t bal = __ballot_sync(0xffffffffu, fix);
+    if (bal == 0u) return;
+    const uint32_t cnt = __popc(bal);
+    if (fq.n + cnt > kFixSlots) fix_drain<Op>(fq, ch);
+    if (fix) {
+        const uint32_t slot = fq.n + __popc(bal & ((1u << (threadIdx.x & 31)) - 1u));
+        fq.v[slot] = make_float4(v[0], v[1], v[2], v[3]);
+        fq.e[slot] = e;
+    }
+    fq.n += cnt;
+}
+
+// Encode and store one quad of FP8 codes at d (reference rules).  DEFER: the
+// fix-up goes through the warp's queue (all 32 lanes must be here); else inline.
+template <int FP8, bool DEFER, class Op>
+__device__ __forceinline__ void fp8_quad_store(const float (&v)[4], uint8_t* d, int64_t e, const ChunkRec& ch,
+                                               FixQueue& fq) {
+    uint32_t o[1];
+    const bool slow = encode4_fp8_fast<FP8>(v, o[0]);
+    if constexpr (DEFER) {
+        if (!slow) store4_stream<1>(d, o);
+        fix_push<Op>(fq, slow, v, e, ch);
+    } else {
+        if (slow) o[0] = encode4_fp8_ref<FP8>(v);
+        store4_stream<1>(d, o);
+    }
+}
+
+template <int FP8>
+__device__ __forceinline__ void fp8_quad_fix(const float4& q, uint8_t* d) {
+    const float v[4] = {q.x, q.y, q.z, q.w};
+    const uint32_t o[1] = {encode4_fp8_ref<FP8>(v)};
+    store4_stream<1>(d, o);
+}
+
 // ----------------------------------------------------------------- ops
+//
+// quad<DEFER>(sp, ch, e, state, fq): elements e .. e+3 of the chunk, whose
+// source bytes are at sp (shared memory).  kDefers: the op parks FP8 fix-ups
+// in the warp queue when DEFER is set and encodes them in fix().
 
 // Plain conversion src -> dst (mf_convert).
 template <int SRC, int DST, int COMPAT>
 struct ConvertOp {
     static constexpr int kIn = dtype_bytes(SRC);
+    static constexpr bool kDefers = (DST == MF_DT_F8E4M3 || DST == MF_DT_F8E5M2) && COMPAT == 0;
     struct State {};
     template <class A>
     __device__ static State setup(const A&, const ChunkRec&) { return {}; }
     template <class A>
     __device__ static void first_tile(const A&, const ChunkRec&) {}
-    // elements e .. e+3 of the chunk; their source bytes are at sp (shared memory)
-    __device__ static void quad(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State&) {
-        uint32_t w[kIn], o[dtype_bytes(DST)];
+    template <bool DEFER>
+    __device__ static void quad(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State&, FixQueue& fq) {
+        uint32_t w[kIn];
         load4<kIn>(sp, w);
         float v[4];
         decode4<SRC>(w, v);
-        encode4<DST>(v, o, COMPAT);
-        store4_stream<dtype_bytes(DST)>(static_cast<uint8_t*>(ch.dst) + e * dtype_bytes(DST), o);
+        uint8_t* d = static_cast<uint8_t*>(ch.dst) + e * dtype_bytes(DST);
+        if constexpr (kDefers) {
+            fp8_quad_store<DST, DEFER, ConvertOp>(v, d, e, ch, fq);
+        } else {
+            uint32_t o[dtype_bytes(DST)];
+            encode4<DST>(v, o, COMPAT);
+            store4_stream<dtype_bytes(DST)>(d, o);
+        }
+    }
+    __device__ static void fix(const ChunkRec& ch, const float4& q, int64_t e) {
+        if constexpr (kDefers) fp8_quad_fix<DST>(q, static_cast<uint8_t*>(ch.dst) + e);
     }
     __device__ static void element(const ChunkRec& ch, int64_t i, const State&) {
         store_code<DST>(ch.dst, i, encode_f32<DST>(load_as_f32<SRC>(ch.src, i), COMPAT));
@@ -162,6 +242,7 @@ __device__ __forceinline__ float scale_inv_from_amax(float amax, int fp8_dtype) 
 template <int SRC, int FP8, int COMPAT>
 struct CastOp {
     static constexpr int kIn = dtype_bytes(SRC);
+    static constexpr bool kDefers = COMPAT == 0;
     struct State {
         float scale;
     };
@@ -173,16 +254,26 @@ struct CastOp {
     __device__ static void first_tile(const A& a, const ChunkRec& ch) {
         if (a.scale_inv) a.scale_inv[ch.tensor] = scale_inv_from_amax(a.amax[ch.tensor], FP8);
     }
-    __device__ static void quad(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State& st) {
-        uint32_t w[kIn], o[1];
+    template <bool DEFER>
+    __device__ static void quad(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State& st, FixQueue& fq) {
+        uint32_t w[kIn];
         load4<kIn>(sp, w);
         float v[4];
         decode4<SRC>(w, v);
         const float2 a = __fmul2_rn(make_float2(v[0], v[1]), make_float2(st.scale, st.scale));
         const float2 b = __fmul2_rn(make_float2(v[2], v[3]), make_float2(st.scale, st.scale));
         const float s[4] = {a.x, a.y, b.x, b.y};
-        encode4<FP8>(s, o, COMPAT);
-        store4_stream<1>(static_cast<uint8_t*>(ch.dst) + e, o);
+        uint8_t* d = static_cast<uint8_t*>(ch.dst) + e;
+        if constexpr (kDefers) {
+            fp8_quad_store<FP8, DEFER, CastOp>(s, d, e, ch, fq);
+        } else {
+            uint32_t o[1];
+            encode4<FP8>(s, o, COMPAT);
+            store4_stream<1>(d, o);
+        }
+    }
+    __device__ static void fix(const ChunkRec& ch, const float4& q, int64_t e) {
+        fp8_quad_fix<FP8>(q, static_cast<uint8_t*>(ch.dst) + e);
     }
     __device__ static void element(const ChunkRec& ch, int64_t i, const State& st) {
         store_code<FP8>(ch.dst, i, encode_f32<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), st.scale), COMPAT));
@@ -195,7 +286,9 @@ template <class Op>
 struct StreamGeometry {
     static constexpr int kTileBytes = static_cast<int>(kTileElems) * Op::kIn;
     static constexpr int kStages = (kStreamSmemBudget / kTileBytes) < 8 ? (kStreamSmemBudget / kTileBytes) : 8;
-    static constexpr int kSmemBytes = kStages * kTileBytes + kStages * 16;
+    static constexpr int kFixOffset = kStages * kTileBytes + kStages * 16;  // 16-byte aligned
+    static constexpr int kFixBytes = Op::kDefers ? kConsumerWarps * kFixSlots * (16 + 8) : 0;
+    static constexpr int kSmemBytes = kFixOffset + kFixBytes;
     static_assert(kStages >= 2, "tile too large for the staging budget");
 };
 
@@ -222,7 +315,6 @@ __device__ __forceinline__ int stream_first_chunk(const StreamArgs<MaxChunks>& a
 //            (1 arrival with the byte count, then the transaction bytes);
 //   empty[s] completes when all 8 consumer warps are done with stage s.
 // Consumers never synchronise with each other, only with the copy engine.
-constexpr int kConsumerWarps = kStreamThreads / 32;
 constexpr int kStreamBlock = kStreamThreads + 32;
 
 template <class Op, int MaxChunks>
@@ -286,6 +378,11 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
 
     // -------------------- consumers: decode, compute, store
     const int lane = threadIdx.x & 31;
+    FixQueue fq;
+    fq.v = reinterpret_cast<float4*>(smem + G::kFixOffset) + (threadIdx.x >> 5) * kFixSlots;
+    fq.e = reinterpret_cast<int64_t*>(smem + G::kFixOffset + kConsumerWarps * kFixSlots * 16) +
+           (threadIdx.x >> 5) * kFixSlots;
+    fq.n = 0;
     int k = stream_first_chunk(a, t0);
     typename Op::State st = Op::setup(a, a.chunk[k]);
     for (int64_t i = 0; i < ntiles; ++i) {
@@ -315,13 +412,16 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
 #pragma unroll
                 for (int j = 0; j < kQuadsPerThread; ++j) {
                     const int q = threadIdx.x + j * kStreamThreads;
-                    Op::quad(tp + q * 4 * Op::kIn, ch, e0 + 4 * q, st);
+                    Op::template quad<Op::kDefers>(tp + q * 4 * Op::kIn, ch, e0 + 4 * q, st, fq);
                 }
+                // parked FP8 fix-ups belong to this chunk: encode them now
+                if constexpr (Op::kDefers)
+                    if (fq.n) fix_drain<Op>(fq, ch);
             } else {
                 const int copied = static_cast<int>(((cnt * Op::kIn) & ~int64_t(15)) / Op::kIn);
                 const int nquads = copied / 4;
                 for (int q = threadIdx.x; q < nquads; q += kStreamThreads)
-                    Op::quad(tp + q * 4 * Op::kIn, ch, e0 + 4 * q, st);
+                    Op::template quad<false>(tp + q * 4 * Op::kIn, ch, e0 + 4 * q, st, fq);
                 const int rem = static_cast<int>(cnt) - nquads * 4;
                 if (threadIdx.x < rem) Op::element(ch, e0 + nquads * 4 + threadIdx.x, st);
             }

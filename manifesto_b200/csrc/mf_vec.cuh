@@ -235,16 +235,45 @@ __device__ __forceinline__ uint32_t encode4_e4m3_ref(float v0, float v1, float v
 // (dtype/fp8.go:190-249): the hardware result unless a value lies in the
 // reference's subnormal band 2^-17 <= |v| < 2^-14, above 57344 (the
 // reference returns Inf) or is NaN; then the exact integer routine.
-__device__ __forceinline__ uint32_t encode4_e5m2_ref(float v0, float v1, float v2, float v3) {
+__device__ __forceinline__ bool e5m2_needs_exact(float v0, float v1, float v2, float v3) {
     const float a[4] = {fabsf(v0), fabsf(v1), fabsf(v2), fabsf(v3)};
     bool slow = false;
 #pragma unroll
     for (int j = 0; j < 4; ++j)
         slow |= ((a[j] >= 7.62939453125e-06f) & (a[j] < 6.103515625e-05f)) | !(a[j] <= 57344.0f);
-    if (slow)
+    return slow;
+}
+
+__device__ __forceinline__ uint32_t encode4_e5m2_ref(float v0, float v1, float v2, float v3) {
+    if (e5m2_needs_exact(v0, v1, v2, v3))
         return f32bits_to_e5m2_ref(__float_as_uint(v0)) | (f32bits_to_e5m2_ref(__float_as_uint(v1)) << 8) |
                (f32bits_to_e5m2_ref(__float_as_uint(v2)) << 16) | (f32bits_to_e5m2_ref(__float_as_uint(v3)) << 24);
     return cvt4_fp8_satfinite<MF_DT_F8E5M2>(v0, v1, v2, v3);
+}
+
+// The common case of the two encoders above, without their fix-up branch:
+// returns false with the reference codes in `out`, or true when the quad
+// needs encode4_e4m3_ref / encode4_e5m2_ref (then `out` is meaningless).
+template <int DT>
+__device__ __forceinline__ bool encode4_fp8_fast(const float (&v)[4], uint32_t& out) {
+    if constexpr (DT == MF_DT_F8E4M3) {
+        const uint32_t c = cvt4_fp8_satfinite<MF_DT_F8E4M3>(v[0], v[1], v[2], v[3]);
+        const uint32_t c7 = c & 0x7f7f7f7fu;
+        const uint32_t big = bytes_from_bit7((c7 + 0x08080808u) & 0x80808080u);  // code >= 0x78
+        out = (c & ~big) | (big & ((c & 0x80808080u) | 0x7e7e7e7eu));
+        // any code in [0, 8] or 0x7f: (code + 1) mod 128 < 10
+        const uint32_t t = ((c7 + 0x01010101u) & 0x7f7f7f7fu) + 0x76767676u;
+        return (~t & 0x80808080u) != 0;
+    } else {
+        out = cvt4_fp8_satfinite<MF_DT_F8E5M2>(v[0], v[1], v[2], v[3]);
+        return e5m2_needs_exact(v[0], v[1], v[2], v[3]);
+    }
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t encode4_fp8_ref(const float (&v)[4]) {
+    if constexpr (DT == MF_DT_F8E4M3) return encode4_e4m3_ref(v[0], v[1], v[2], v[3]);
+    else return encode4_e5m2_ref(v[0], v[1], v[2], v[3]);
 }
 
 // Decode one quad (raw words w[0 .. bytes-1]) of a floating storage format.

@@ -266,6 +266,35 @@ def test_fp8_quantize_bit_exact(backend, ref, src, fp8, compat):
         b.free()
 
 
+@pytest.mark.parametrize("fp8", [E4M3, E5M2])
+@pytest.mark.parametrize("src", [F32, BF16])
+def test_scaled_cast_fixup_heavy(backend, ref, src, fp8):
+    """Scaled casts where most quads need the exact encoder (subnormal bands, the
+    E4M3 2^-10 tie, NaN, E5M2 overflow): whole tiles where every warp parks more
+    quads than its queue holds, next to tiles with none, plus a ragged end."""
+    rng = np.random.default_rng(int(src) * 16 + int(fp8))
+    n = 40 * 8192 + 13
+    lo, hi = (2.0 ** -11, 2.0 ** -5) if fp8 == E4M3 else (2.0 ** -18, 2.0 ** -13)
+    mag = np.exp2(rng.uniform(np.log2(lo), np.log2(hi), n)).astype(np.float32)
+    v = np.where(rng.random(n) < 0.5, -mag, mag).astype(np.float32)
+    v[8192 * 3: 8192 * 5] = rng.standard_normal(8192 * 2).astype(np.float32) * 100.0  # tiles with few fix-ups
+    v[::97] = 2.0 ** -10
+    v[::101] = -(2.0 ** -10)
+    v[::389] = np.nan
+    v[::211] = 0.0
+    v[::503] = 60000.0  # past both formats' maxima: E4M3 saturates, E5M2 gives the reference's Inf
+    raw = v if src == F32 else synthetic.f32_to_bf16_bits(v)
+    amax = 448.0 if fp8 == E4M3 else 57344.0  # scale exactly 1: the values above land unscaled
+    d = to_device(raw)
+    q = empty(n)
+    am = to_device(np.array([amax], np.float32))
+    for compat in (0, 1):
+        call("mf_fp8_scaled_cast", d.ptr, src, q.ptr, fp8, am.ptr, None, n, compat, None)
+        bits_equal(fetch(q, n), ref.scaled_cast(raw, src, fp8, amax, compat, threads=host_threads()))
+    for b in (d, q, am):
+        b.free()
+
+
 def test_quantize_zero_and_tiny(backend, ref):
     n = 4096
     raw = np.zeros(n, np.uint16)

@@ -252,7 +252,7 @@ def _kernel_c2(torch, stream_handle, peak, flush, reps) -> dict:
                      stream_handle)
     _warm(f)
     b = rows * cols // 2 + sc.numel() * 2 + rows * cols * 2
-    return {"c2_int4_to_bf16": kernel_line("int4_dequant_words_kernel<BF16,BF16>", b,
+    return {"c2_int4_to_bf16": kernel_line("int4_dequant_flat_kernel<BF16,BF16>", b,
                                            time_launches(torch, f, reps, flush), peak, rows * cols)}
 
 

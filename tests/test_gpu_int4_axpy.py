@@ -34,7 +34,7 @@ def test_int4_config2_full_shape(backend, ref):
 
 
 @pytest.mark.parametrize("rows,cols,group", [(1, 32, 32), (3, 64, 32), (7, 256, 128), (5, 96, 48), (2, 10, 4),
-                                             (4, 130, 128), (1, 2, 1)])
+                                             (4, 130, 128), (1, 2, 1), (3, 136, 64), (300, 2048, 256)])
 @pytest.mark.parametrize("sdt,odt", [(BF16, BF16), (F16, F32), (F32, F16), (F32, BF16)])
 def test_int4_shapes_and_dtypes(backend, ref, rows, cols, group, sdt, odt):
     q = synthetic.uniform_bytes(rows * 1000 + cols, rows * cols // 2)

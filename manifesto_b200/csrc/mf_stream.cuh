@@ -123,20 +123,77 @@ __device__ __forceinline__ void load_raw_smem(const uint8_t* tile, int c, RawChu
     }
 }
 
+// ------------------------------------------------------------ lane steps
+//
+// In one step a lane owns kLane consecutive elements (4 or 8) and lane l of
+// a warp owns run r0 + l, so a warp step reads and writes one contiguous span
+// and every shared and global access is a full vector.  kLane is 8 when both
+// element widths are at most 2 bytes (one 16-byte shared read, at most 16
+// bytes stored per lane), else 4: a wider per-lane run would split each
+// warp's vector accesses over twice the span (half-filled sectors on the
+// store side, two-way bank conflicts on the shared side).
+template <int InBytes, int OutBytes>
+constexpr int lane_elems() { return (InBytes <= 2 && OutBytes <= 2) ? 8 : 4; }
+
+// Bytes (4, 8, 16 or 32) of source elements at p in shared memory -> w.
+template <int Bytes>
+__device__ __forceinline__ void load_lane_smem(const uint8_t* p, uint32_t (&w)[Bytes / 4]) {
+    if constexpr (Bytes == 4) {
+        w[0] = *reinterpret_cast<const uint32_t*>(p);
+    } else if constexpr (Bytes == 8) {
+        const uint2 x = *reinterpret_cast<const uint2*>(p);
+        w[0] = x.x;
+        w[1] = x.y;
+    } else {
+#pragma unroll
+        for (int k = 0; k < Bytes / 16; ++k) {
+            const uint4 x = reinterpret_cast<const uint4*>(p)[k];
+            w[4 * k + 0] = x.x;
+            w[4 * k + 1] = x.y;
+            w[4 * k + 2] = x.z;
+            w[4 * k + 3] = x.w;
+        }
+    }
+}
+
+// Bytes (4, 8, 16 or 32) of encoded elements from w to global memory, streaming stores.
+template <int Bytes>
+__device__ __forceinline__ void store_lane_stream(void* p, const uint32_t (&w)[Bytes / 4]) {
+    if constexpr (Bytes == 4) {
+        asm volatile("st.global.cs.u32 [%0], %1;" ::"l"(p), "r"(w[0]) : "memory");
+    } else if constexpr (Bytes == 8) {
+        asm volatile("st.global.cs.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(w[0]), "r"(w[1]) : "memory");
+    } else {
+#pragma unroll
+        for (int k = 0; k < Bytes / 16; ++k)
+            st_stream(static_cast<uint4*>(p) + k, make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]));
+    }
+}
+
+// Load and decode one lane step: v[k] = elements 4k .. 4k+3 (k < Q = kLane / 4).
+template <int SRC, int Q>
+__device__ __forceinline__ void load_decode_lane(const uint8_t* sp, float (&v)[2][4]) {
+    constexpr int kIn = dtype_bytes(SRC);
+    uint32_t w[Q * kIn];
+    load_lane_smem<4 * Q * kIn>(sp, w);
+#pragma unroll
+    for (int k = 0; k < Q; ++k) decode4<SRC>(w + k * kIn, v[k]);
+}
+
 // ------------------------------------------------------ deferred fix-ups
 //
 // The reference's FP8 encoders differ from the hardware conversion on a few
 // value classes (E4M3: NaN, the subnormal band, 2^-10 exactly; E5M2: NaN, the
 // subnormal band, overflow).  On data with many values near zero (activations)
-// a quarter to half of all warp-wide quad steps hold at least one such value,
-// and fixing it inline makes the whole warp run the fix-up.  Instead each warp
-// parks the quads that need it in a 32-slot shared-memory queue (ballot +
-// prefix count; the lane skips its store) and encodes the parked quads
-// together at the end of the tile, one quad per lane.
+// a quarter to half of all warp steps hold at least one such value, and
+// fixing it inline makes the whole warp run the fix-up.  Instead each warp
+// parks the lane steps that need it in a 32-slot shared-memory queue (ballot
+// + prefix count; the lane skips its store) and encodes the parked steps
+// together at the end of the tile, one per lane.
 constexpr int kFixSlots = 32;
 
 struct FixQueue {
-    float4* v;   // this warp's slots: a parked quad's four values
+    float4* v;   // this warp's slots: slot i holds a parked step's values in v[2i] (and v[2i+1] for 8 elements)
     int64_t* e;  // and its first element index within the chunk
     uint32_t n;  // filled slots (warp-uniform)
 };
@@ -145,59 +202,71 @@ template <class Op>
 __device__ __forceinline__ void fix_drain(FixQueue& fq, const ChunkRec& ch) {
     __syncwarp();
     const uint32_t lane = threadIdx.x & 31;
-    if (lane < fq.n) Op::fix(ch, fq.v[lane], fq.e[lane]);
+    if (lane < fq.n) Op::fix(ch, fq.v[2 * lane], fq.v[2 * lane + 1], fq.e[lane]);
     __syncwarp();
     fq.n = 0;
 }
 
-// Warp-collective (all 32 lanes): park this lane's quad when `fix` is set.
-template <class Op>
-__device__ __forceinline__ void fix_push(FixQueue& fq, bool fix, const float (&v)[4], int64_t e, const ChunkRec& ch) {
+// Warp-collective (all 32 lanes): park this lane's step when `fix` is set.
+template <class Op, int Q>
+__device__ __forceinline__ void fix_push(FixQueue& fq, bool fix, const float (&v)[2][4], int64_t e,
+                                         const ChunkRec& ch) {
     const uint32_t bal = __ballot_sync(0xffffffffu, fix);
     if (bal == 0u) return;
     const uint32_t cnt = __popc(bal);
     if (fq.n + cnt > kFixSlots) fix_drain<Op>(fq, ch);
     if (fix) {
         const uint32_t slot = fq.n + __popc(bal & ((1u << (threadIdx.x & 31)) - 1u));
-        fq.v[slot] = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+        for (int k = 0; k < Q; ++k) fq.v[2 * slot + k] = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
         fq.e[slot] = e;
     }
     fq.n += cnt;
 }
 
-// Encode and store one quad of FP8 codes at d (reference rules).  DEFER: the
-// fix-up goes through the warp's queue (all 32 lanes must be here); else inline.
-template <int FP8, bool DEFER, class Op>
-__device__ __forceinline__ void fp8_quad_store(const float (&v)[4], uint8_t* d, int64_t e, const ChunkRec& ch,
+// Encode and store one lane step of FP8 codes at d (reference rules).  DEFER:
+// the fix-up goes through the warp's queue (all 32 lanes must be here); else inline.
+template <int FP8, int Q, bool DEFER, class Op>
+__device__ __forceinline__ void fp8_lane_store(const float (&v)[2][4], uint8_t* d, int64_t e, const ChunkRec& ch,
                                                FixQueue& fq) {
-    uint32_t o[1];
-    const bool slow = encode4_fp8_fast<FP8>(v, o[0]);
+    uint32_t o[Q];
+    uint32_t slow = 0u;
+#pragma unroll
+    for (int k = 0; k < Q; ++k) slow |= encode4_fp8_fast<FP8>(v[k], o[k]);
     if constexpr (DEFER) {
-        if (!slow) store4_stream<1>(d, o);
-        fix_push<Op>(fq, slow, v, e, ch);
+        if (!slow) store_lane_stream<4 * Q>(d, o);
+        fix_push<Op, Q>(fq, slow != 0u, v, e, ch);
     } else {
-        if (slow) o[0] = encode4_fp8_ref<FP8>(v);
-        store4_stream<1>(d, o);
+        if (slow) {
+#pragma unroll
+            for (int k = 0; k < Q; ++k) o[k] = encode4_fp8_ref<FP8>(v[k]);
+        }
+        store_lane_stream<4 * Q>(d, o);
     }
 }
 
-template <int FP8>
-__device__ __forceinline__ void fp8_quad_fix(const float4& q, uint8_t* d) {
-    const float v[4] = {q.x, q.y, q.z, q.w};
-    const uint32_t o[1] = {encode4_fp8_ref<FP8>(v)};
-    store4_stream<1>(d, o);
+template <int FP8, int Q>
+__device__ __forceinline__ void fp8_lane_fix(const float4& a, const float4& b, uint8_t* d) {
+    const float v[2][4] = {{a.x, a.y, a.z, a.w}, {b.x, b.y, b.z, b.w}};
+    uint32_t o[Q];
+#pragma unroll
+    for (int k = 0; k < Q; ++k) o[k] = encode4_fp8_ref<FP8>(v[k]);
+    store_lane_stream<4 * Q>(d, o);
 }
 
 // ----------------------------------------------------------------- ops
 //
-// quad<DEFER>(sp, ch, e, state, fq): elements e .. e+3 of the chunk, whose
-// source bytes are at sp (shared memory).  kDefers: the op parks FP8 fix-ups
-// in the warp queue when DEFER is set and encodes them in fix().
+// step<DEFER>(sp, ch, e, state, fq): elements e .. e+kLane-1 of the chunk,
+// whose source bytes are at sp (shared memory).  kDefers: the op parks FP8
+// fix-ups in the warp queue when DEFER is set and encodes them in fix().
 
 // Plain conversion src -> dst (mf_convert).
 template <int SRC, int DST, int COMPAT>
 struct ConvertOp {
     static constexpr int kIn = dtype_bytes(SRC);
+    static constexpr int kOut = dtype_bytes(DST);
+    static constexpr int kLane = lane_elems<kIn, kOut>();
+    static constexpr int kQ = kLane / 4;
     static constexpr bool kDefers = (DST == MF_DT_F8E4M3 || DST == MF_DT_F8E5M2) && COMPAT == 0;
     struct State {};
     template <class A>
@@ -205,22 +274,21 @@ struct ConvertOp {
     template <class A>
     __device__ static void first_tile(const A&, const ChunkRec&) {}
     template <bool DEFER>
-    __device__ static void quad(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State&, FixQueue& fq) {
-        uint32_t w[kIn];
-        load4<kIn>(sp, w);
-        float v[4];
-        decode4<SRC>(w, v);
-        uint8_t* d = static_cast<uint8_t*>(ch.dst) + e * dtype_bytes(DST);
+    __device__ static void step(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State&, FixQueue& fq) {
+        float v[2][4];
+        load_decode_lane<SRC, kQ>(sp, v);
+        uint8_t* d = static_cast<uint8_t*>(ch.dst) + e * kOut;
         if constexpr (kDefers) {
-            fp8_quad_store<DST, DEFER, ConvertOp>(v, d, e, ch, fq);
+            fp8_lane_store<DST, kQ, DEFER, ConvertOp>(v, d, e, ch, fq);
         } else {
-            uint32_t o[dtype_bytes(DST)];
-            encode4<DST>(v, o, COMPAT);
-            store4_stream<dtype_bytes(DST)>(d, o);
+            uint32_t o[kQ * kOut];
+#pragma unroll
+            for (int k = 0; k < kQ; ++k) encode4<DST>(v[k], o + k * kOut, COMPAT);
+            store_lane_stream<kLane * kOut>(d, o);
         }
     }
-    __device__ static void fix(const ChunkRec& ch, const float4& q, int64_t e) {
-        if constexpr (kDefers) fp8_quad_fix<DST>(q, static_cast<uint8_t*>(ch.dst) + e);
+    __device__ static void fix(const ChunkRec& ch, const float4& a, const float4& b, int64_t e) {
+        if constexpr (kDefers) fp8_lane_fix<DST, kQ>(a, b, static_cast<uint8_t*>(ch.dst) + e);
     }
     __device__ static void element(const ChunkRec& ch, int64_t i, const State&) {
         store_code<DST>(ch.dst, i, encode_f32<DST>(load_as_f32<SRC>(ch.src, i), COMPAT));
@@ -238,10 +306,21 @@ __device__ __forceinline__ float scale_inv_from_amax(float amax, int fp8_dtype) 
     return ok ? __fdiv_rn(amax, fp8_max_of(fp8_dtype)) : 1.0f;
 }
 
+__device__ __forceinline__ void scale4(float (&v)[4], float s) {
+    const float2 a = __fmul2_rn(make_float2(v[0], v[1]), make_float2(s, s));
+    const float2 b = __fmul2_rn(make_float2(v[2], v[3]), make_float2(s, s));
+    v[0] = a.x;
+    v[1] = a.y;
+    v[2] = b.x;
+    v[3] = b.y;
+}
+
 // Per-tensor amax-scaled FP8 cast: q = encode(v * (fp8_max / amax[tensor])).
 template <int SRC, int FP8, int COMPAT>
 struct CastOp {
     static constexpr int kIn = dtype_bytes(SRC);
+    static constexpr int kLane = lane_elems<kIn, 1>();
+    static constexpr int kQ = kLane / 4;
     static constexpr bool kDefers = COMPAT == 0;
     struct State {
         float scale;
@@ -255,25 +334,23 @@ struct CastOp {
         if (a.scale_inv) a.scale_inv[ch.tensor] = scale_inv_from_amax(a.amax[ch.tensor], FP8);
     }
     template <bool DEFER>
-    __device__ static void quad(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State& st, FixQueue& fq) {
-        uint32_t w[kIn];
-        load4<kIn>(sp, w);
-        float v[4];
-        decode4<SRC>(w, v);
-        const float2 a = __fmul2_rn(make_float2(v[0], v[1]), make_float2(st.scale, st.scale));
-        const float2 b = __fmul2_rn(make_float2(v[2], v[3]), make_float2(st.scale, st.scale));
-        const float s[4] = {a.x, a.y, b.x, b.y};
+    __device__ static void step(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State& st, FixQueue& fq) {
+        float v[2][4];
+        load_decode_lane<SRC, kQ>(sp, v);
+#pragma unroll
+        for (int k = 0; k < kQ; ++k) scale4(v[k], st.scale);
         uint8_t* d = static_cast<uint8_t*>(ch.dst) + e;
         if constexpr (kDefers) {
-            fp8_quad_store<FP8, DEFER, CastOp>(s, d, e, ch, fq);
+            fp8_lane_store<FP8, kQ, DEFER, CastOp>(v, d, e, ch, fq);
         } else {
-            uint32_t o[1];
-            encode4<FP8>(s, o, COMPAT);
-            store4_stream<1>(d, o);
+            uint32_t o[kQ];
+#pragma unroll
+            for (int k = 0; k < kQ; ++k) encode4<FP8>(v[k], o + k, COMPAT);
+            store_lane_stream<4 * kQ>(d, o);
         }
     }
-    __device__ static void fix(const ChunkRec& ch, const float4& q, int64_t e) {
-        fp8_quad_fix<FP8>(q, static_cast<uint8_t*>(ch.dst) + e);
+    __device__ static void fix(const ChunkRec& ch, const float4& a, const float4& b, int64_t e) {
+        fp8_lane_fix<FP8, kQ>(a, b, static_cast<uint8_t*>(ch.dst) + e);
     }
     __device__ static void element(const ChunkRec& ch, int64_t i, const State& st) {
         store_code<FP8>(ch.dst, i, encode_f32<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), st.scale), COMPAT));
@@ -287,7 +364,7 @@ struct StreamGeometry {
     static constexpr int kTileBytes = static_cast<int>(kTileElems) * Op::kIn;
     static constexpr int kStages = (kStreamSmemBudget / kTileBytes) < 8 ? (kStreamSmemBudget / kTileBytes) : 8;
     static constexpr int kFixOffset = kStages * kTileBytes + kStages * 16;  // 16-byte aligned
-    static constexpr int kFixBytes = Op::kDefers ? kConsumerWarps * kFixSlots * (16 + 8) : 0;
+    static constexpr int kFixBytes = Op::kDefers ? kConsumerWarps * kFixSlots * (32 + 8) : 0;
     static constexpr int kSmemBytes = kFixOffset + kFixBytes;
     static_assert(kStages >= 2, "tile too large for the staging budget");
 };
@@ -379,8 +456,8 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
     // -------------------- consumers: decode, compute, store
     const int lane = threadIdx.x & 31;
     FixQueue fq;
-    fq.v = reinterpret_cast<float4*>(smem + G::kFixOffset) + (threadIdx.x >> 5) * kFixSlots;
-    fq.e = reinterpret_cast<int64_t*>(smem + G::kFixOffset + kConsumerWarps * kFixSlots * 16) +
+    fq.v = reinterpret_cast<float4*>(smem + G::kFixOffset) + (threadIdx.x >> 5) * 2 * kFixSlots;
+    fq.e = reinterpret_cast<int64_t*>(smem + G::kFixOffset + kConsumerWarps * kFixSlots * 32) +
            (threadIdx.x >> 5) * kFixSlots;
     fq.n = 0;
     int k = stream_first_chunk(a, t0);
@@ -402,28 +479,28 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
         }
         if (tile == 0 && threadIdx.x == 0) Op::first_tile(a, ch);
         if (ch.aligned) {
-            // lane-consecutive quads: every warp access is one contiguous span
+            // lane-consecutive runs: every warp access is one contiguous span
             // only the first ((cnt * kIn) & ~15) bytes were copied (16-byte
             // granularity); the elements past them come from global memory
             const uint8_t* tp = smem + s * G::kTileBytes;
             if (cnt == kTileElems) {
                 // full tile: a fixed trip count, unrolled
-                constexpr int kQuadsPerThread = static_cast<int>(kTileElems / 4 / kStreamThreads);
+                constexpr int kStepsPerThread = static_cast<int>(kTileElems / Op::kLane / kStreamThreads);
 #pragma unroll
-                for (int j = 0; j < kQuadsPerThread; ++j) {
+                for (int j = 0; j < kStepsPerThread; ++j) {
                     const int q = threadIdx.x + j * kStreamThreads;
-                    Op::template quad<Op::kDefers>(tp + q * 4 * Op::kIn, ch, e0 + 4 * q, st, fq);
+                    Op::template step<Op::kDefers>(tp + q * Op::kLane * Op::kIn, ch, e0 + Op::kLane * q, st, fq);
                 }
                 // parked FP8 fix-ups belong to this chunk: encode them now
                 if constexpr (Op::kDefers)
                     if (fq.n) fix_drain<Op>(fq, ch);
             } else {
                 const int copied = static_cast<int>(((cnt * Op::kIn) & ~int64_t(15)) / Op::kIn);
-                const int nquads = copied / 4;
-                for (int q = threadIdx.x; q < nquads; q += kStreamThreads)
-                    Op::template quad<false>(tp + q * 4 * Op::kIn, ch, e0 + 4 * q, st, fq);
-                const int rem = static_cast<int>(cnt) - nquads * 4;
-                if (threadIdx.x < rem) Op::element(ch, e0 + nquads * 4 + threadIdx.x, st);
+                const int nsteps = copied / Op::kLane;
+                for (int q = threadIdx.x; q < nsteps; q += kStreamThreads)
+                    Op::template step<false>(tp + q * Op::kLane * Op::kIn, ch, e0 + Op::kLane * q, st, fq);
+                const int rem = static_cast<int>(cnt) - nsteps * Op::kLane;
+                if (threadIdx.x < rem) Op::element(ch, e0 + nsteps * Op::kLane + threadIdx.x, st);
             }
         } else {
             for (int64_t j = e0 + threadIdx.x; j < e0 + cnt; j += kStreamThreads) Op::element(ch, j, st);
@@ -439,16 +516,25 @@ int* sticky_status_ptr();
 template <class Op, int MaxChunks>
 inline cudaError_t launch_stream(const StreamArgs<MaxChunks>& a, int sm_count, cudaStream_t s) {
     using G = StreamGeometry<Op>;
-    static int attr_done[64] = {0};  // per device: dynamic shared memory opt-in done
+    // per device: resident CTAs per SM after the dynamic shared memory opt-in (0 = not set up yet)
+    static int per_sm[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(stream_kernel<Op, MaxChunks>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes);
-        if (e != cudaSuccess) return e;
-        attr_done[dev] = 1;
+    int resident = 3;
+    if (dev >= 0 && dev < 64) {
+        if (!per_sm[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(stream_kernel<Op, MaxChunks>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes);
+            if (e != cudaSuccess) return e;
+            int occ = 0;
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, stream_kernel<Op, MaxChunks>, kStreamBlock,
+                                                              G::kSmemBytes);
+            if (e != cudaSuccess) return e;
+            per_sm[dev] = occ < 1 ? 1 : (occ > 3 ? 3 : occ);
+        }
+        resident = per_sm[dev];
     }
-    int64_t blocks = static_cast<int64_t>(sm_count) * 3;
+    int64_t blocks = static_cast<int64_t>(sm_count) * resident;
     if (a.total_tiles < blocks) blocks = a.total_tiles;
     if (blocks < 1) return cudaSuccess;
     stream_kernel<Op, MaxChunks><<<static_cast<unsigned>(blocks), kStreamBlock, G::kSmemBytes, s>>>(a);

@@ -251,22 +251,32 @@ __device__ __forceinline__ uint32_t encode4_e5m2_ref(float v0, float v1, float v
     return cvt4_fp8_satfinite<MF_DT_F8E5M2>(v0, v1, v2, v3);
 }
 
+// 0xff in every byte of x whose bit 7 is set, 0x00 in the others: one byte
+// permute with sign replication (selector nibble 8 + k copies the sign of
+// byte k over all 8 bits of target byte k).
+__device__ __forceinline__ uint32_t bytes_sign_mask(uint32_t x) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, 0, 0xBA98;" : "=r"(r) : "r"(x));
+    return r;
+}
+
 // The common case of the two encoders above, without their fix-up branch:
-// returns false with the reference codes in `out`, or true when the quad
+// returns the reference codes in `out` and a nonzero flag word when the quad
 // needs encode4_e4m3_ref / encode4_e5m2_ref (then `out` is meaningless).
+// Every byte sum below stays under 0x100 (codes have magnitude <= 0x7f), so no
+// carry crosses a byte.
 template <int DT>
-__device__ __forceinline__ bool encode4_fp8_fast(const float (&v)[4], uint32_t& out) {
+__device__ __forceinline__ uint32_t encode4_fp8_fast(const float (&v)[4], uint32_t& out) {
     if constexpr (DT == MF_DT_F8E4M3) {
         const uint32_t c = cvt4_fp8_satfinite<MF_DT_F8E4M3>(v[0], v[1], v[2], v[3]);
         const uint32_t c7 = c & 0x7f7f7f7fu;
-        const uint32_t big = bytes_from_bit7((c7 + 0x08080808u) & 0x80808080u);  // code >= 0x78
+        const uint32_t big = bytes_sign_mask(c7 + 0x08080808u);  // code >= 0x78: the reference's 0x7e
         out = (c & ~big) | (big & ((c & 0x80808080u) | 0x7e7e7e7eu));
-        // any code in [0, 8] or 0x7f: (code + 1) mod 128 < 10
-        const uint32_t t = ((c7 + 0x01010101u) & 0x7f7f7f7fu) + 0x76767676u;
-        return (~t & 0x80808080u) != 0;
+        // code <= 8 (c7 + 0x77 < 0x80) or NaN 0x7f (c7 + 0x01 == 0x80)
+        return (~(c7 + 0x77777777u) | (c7 + 0x01010101u)) & 0x80808080u;
     } else {
         out = cvt4_fp8_satfinite<MF_DT_F8E5M2>(v[0], v[1], v[2], v[3]);
-        return e5m2_needs_exact(v[0], v[1], v[2], v[3]);
+        return e5m2_needs_exact(v[0], v[1], v[2], v[3]) ? 1u : 0u;
     }
 }
 

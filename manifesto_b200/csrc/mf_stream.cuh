@@ -189,37 +189,38 @@ __device__ __forceinline__ void load_decode_lane(const uint8_t* sp, float (&v)[2
 // fixing it inline makes the whole warp run the fix-up.  Instead each warp
 // parks the lane steps that need it in a 32-slot shared-memory queue (ballot
 // + prefix count; the lane skips its store) and encodes the parked steps
-// together at the end of the tile, one per lane.
+// together, one per lane, at the end of each tile (or when the queue is
+// full).  A slot keeps its destination address.
 constexpr int kFixSlots = 32;
 
 struct FixQueue {
-    float4* v;   // this warp's slots: slot i holds a parked step's values in v[2i] (and v[2i+1] for 8 elements)
-    int64_t* e;  // and its first element index within the chunk
-    uint32_t n;  // filled slots (warp-uniform)
+    float4* v;    // this warp's slots: slot i holds a parked step's values in v[2i] (and v[2i+1] for 8 elements)
+    uint8_t** d;  // and where its codes go
+    uint32_t n;   // filled slots (warp-uniform)
 };
 
+// Warp-collective: encode and store every parked step.
 template <class Op>
-__device__ __forceinline__ void fix_drain(FixQueue& fq, const ChunkRec& ch) {
+__device__ __forceinline__ void fix_drain(FixQueue& fq) {
     __syncwarp();
     const uint32_t lane = threadIdx.x & 31;
-    if (lane < fq.n) Op::fix(ch, fq.v[2 * lane], fq.v[2 * lane + 1], fq.e[lane]);
+    if (lane < fq.n) Op::fix(fq.v[2 * lane], fq.v[2 * lane + 1], fq.d[lane]);
     __syncwarp();
     fq.n = 0;
 }
 
 // Warp-collective (all 32 lanes): park this lane's step when `fix` is set.
 template <class Op, int Q>
-__device__ __forceinline__ void fix_push(FixQueue& fq, bool fix, const float (&v)[2][4], int64_t e,
-                                         const ChunkRec& ch) {
+__device__ __forceinline__ void fix_push(FixQueue& fq, bool fix, const float (&v)[2][4], uint8_t* d) {
     const uint32_t bal = __ballot_sync(0xffffffffu, fix);
     if (bal == 0u) return;
     const uint32_t cnt = __popc(bal);
-    if (fq.n + cnt > kFixSlots) fix_drain<Op>(fq, ch);
+    if (fq.n + cnt > kFixSlots) fix_drain<Op>(fq);
     if (fix) {
         const uint32_t slot = fq.n + __popc(bal & ((1u << (threadIdx.x & 31)) - 1u));
 #pragma unroll
         for (int k = 0; k < Q; ++k) fq.v[2 * slot + k] = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
-        fq.e[slot] = e;
+        fq.d[slot] = d;
     }
     fq.n += cnt;
 }
@@ -227,15 +228,14 @@ __device__ __forceinline__ void fix_push(FixQueue& fq, bool fix, const float (&v
 // Encode and store one lane step of FP8 codes at d (reference rules).  DEFER:
 // the fix-up goes through the warp's queue (all 32 lanes must be here); else inline.
 template <int FP8, int Q, bool DEFER, class Op>
-__device__ __forceinline__ void fp8_lane_store(const float (&v)[2][4], uint8_t* d, int64_t e, const ChunkRec& ch,
-                                               FixQueue& fq) {
+__device__ __forceinline__ void fp8_lane_store(const float (&v)[2][4], uint8_t* d, FixQueue& fq) {
     uint32_t o[Q];
     uint32_t slow = 0u;
 #pragma unroll
     for (int k = 0; k < Q; ++k) slow |= encode4_fp8_fast<FP8>(v[k], o[k]);
     if constexpr (DEFER) {
         if (!slow) store_lane_stream<4 * Q>(d, o);
-        fix_push<Op, Q>(fq, slow != 0u, v, e, ch);
+        fix_push<Op, Q>(fq, slow != 0u, v, d);
     } else {
         if (slow) {
 #pragma unroll
@@ -279,7 +279,7 @@ struct ConvertOp {
         load_decode_lane<SRC, kQ>(sp, v);
         uint8_t* d = static_cast<uint8_t*>(ch.dst) + e * kOut;
         if constexpr (kDefers) {
-            fp8_lane_store<DST, kQ, DEFER, ConvertOp>(v, d, e, ch, fq);
+            fp8_lane_store<DST, kQ, DEFER, ConvertOp>(v, d, fq);
         } else {
             uint32_t o[kQ * kOut];
 #pragma unroll
@@ -287,8 +287,8 @@ struct ConvertOp {
             store_lane_stream<kLane * kOut>(d, o);
         }
     }
-    __device__ static void fix(const ChunkRec& ch, const float4& a, const float4& b, int64_t e) {
-        if constexpr (kDefers) fp8_lane_fix<DST, kQ>(a, b, static_cast<uint8_t*>(ch.dst) + e);
+    __device__ static void fix(const float4& a, const float4& b, uint8_t* d) {
+        if constexpr (kDefers) fp8_lane_fix<DST, kQ>(a, b, d);
     }
     __device__ static void element(const ChunkRec& ch, int64_t i, const State&) {
         store_code<DST>(ch.dst, i, encode_f32<DST>(load_as_f32<SRC>(ch.src, i), COMPAT));
@@ -341,7 +341,7 @@ struct CastOp {
         for (int k = 0; k < kQ; ++k) scale4(v[k], st.scale);
         uint8_t* d = static_cast<uint8_t*>(ch.dst) + e;
         if constexpr (kDefers) {
-            fp8_lane_store<FP8, kQ, DEFER, CastOp>(v, d, e, ch, fq);
+            fp8_lane_store<FP8, kQ, DEFER, CastOp>(v, d, fq);
         } else {
             uint32_t o[kQ];
 #pragma unroll
@@ -349,9 +349,7 @@ struct CastOp {
             store_lane_stream<4 * kQ>(d, o);
         }
     }
-    __device__ static void fix(const ChunkRec& ch, const float4& a, const float4& b, int64_t e) {
-        fp8_lane_fix<FP8, kQ>(a, b, static_cast<uint8_t*>(ch.dst) + e);
-    }
+    __device__ static void fix(const float4& a, const float4& b, uint8_t* d) { fp8_lane_fix<FP8, kQ>(a, b, d); }
     __device__ static void element(const ChunkRec& ch, int64_t i, const State& st) {
         store_code<FP8>(ch.dst, i, encode_f32<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), st.scale), COMPAT));
     }
@@ -457,7 +455,7 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
     const int lane = threadIdx.x & 31;
     FixQueue fq;
     fq.v = reinterpret_cast<float4*>(smem + G::kFixOffset) + (threadIdx.x >> 5) * 2 * kFixSlots;
-    fq.e = reinterpret_cast<int64_t*>(smem + G::kFixOffset + kConsumerWarps * kFixSlots * 32) +
+    fq.d = reinterpret_cast<uint8_t**>(smem + G::kFixOffset + kConsumerWarps * kFixSlots * 32) +
            (threadIdx.x >> 5) * kFixSlots;
     fq.n = 0;
     int k = stream_first_chunk(a, t0);
@@ -473,8 +471,9 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
         const int64_t tile = t - ch.tile_begin;
         const int64_t e0 = tile * kTileElems;
         const int64_t cnt = min(kTileElems, ch.n - e0);
-        if (!mbar_wait(&full[s], static_cast<uint32_t>((i / G::kStages) & 1))) {
-            atomicExch(a.status, kDeviceTimeout);
+        // warp-uniform outcome: the lanes meet again in warp-collective fix-up code
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], static_cast<uint32_t>((i / G::kStages) & 1)))) {
+            if (lane == 0) atomicExch(a.status, kDeviceTimeout);
             return;  // the producer's own bounded waits end the CTA
         }
         if (tile == 0 && threadIdx.x == 0) Op::first_tile(a, ch);
@@ -491,9 +490,11 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
                     const int q = threadIdx.x + j * kStreamThreads;
                     Op::template step<Op::kDefers>(tp + q * Op::kLane * Op::kIn, ch, e0 + Op::kLane * q, st, fq);
                 }
-                // parked FP8 fix-ups belong to this chunk: encode them now
+                // fill the holes parked steps left in this tile's output while its
+                // lines are still in L2 (measured faster than letting the queue
+                // fill over several tiles)
                 if constexpr (Op::kDefers)
-                    if (fq.n) fix_drain<Op>(fq, ch);
+                    if (fq.n) fix_drain<Op>(fq);
             } else {
                 const int copied = static_cast<int>(((cnt * Op::kIn) & ~int64_t(15)) / Op::kIn);
                 const int nsteps = copied / Op::kLane;
@@ -508,6 +509,9 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
+    // FP8 fix-ups still parked (every warp leaves the loop after the same tiles)
+    if constexpr (Op::kDefers)
+        if (fq.n) fix_drain<Op>(fq);
 }
 
 // Host side: launch the engine over a filled argument block.

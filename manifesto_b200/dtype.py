@@ -63,6 +63,21 @@ class DType(enum.IntEnum):
         """numpy dtype holding the raw storage codes of one element."""
         return _NP[self]
 
+    def wire_name(self) -> str:
+        """DType.String (dtype/dtype.go:185-232): the uppercase serialised identifier."""
+        return _WIRE.get(self, f"DTYPE({int(self)})")
+
+
+def parse(name: str) -> DType:
+    """dtype.Parse (dtype/dtype.go:234-290): SafeTensors-style uppercase names, the
+    lowercase forms and the aliases, ignoring case, '_' and '-' ("F8_E4M3" is
+    FLOAT8_E4M3).  Raises ValueError for an unknown name."""
+    key = name.strip().upper().replace("_", "").replace("-", "")
+    for dt, names in _PARSE.items():
+        if key in names:
+            return dt
+    raise ValueError(f'dtype: unknown dtype name "{name}"')
+
 
 _SIZE = {
     DType.INVALID: 0, DType.FLOAT64: 8, DType.FLOAT32: 4, DType.FLOAT16: 2, DType.BFLOAT16: 2,
@@ -77,6 +92,25 @@ _NP = {
     DType.INT64: np.dtype(np.int64), DType.INT32: np.dtype(np.int32), DType.INT16: np.dtype(np.int16),
     DType.INT8: np.dtype(np.int8), DType.INT4: np.dtype(np.uint8), DType.UINT64: np.dtype(np.uint64),
     DType.UINT32: np.dtype(np.uint32), DType.UINT16: np.dtype(np.uint16), DType.UINT8: np.dtype(np.uint8),
+}
+
+_WIRE = {
+    DType.FLOAT64: "F64", DType.FLOAT32: "F32", DType.FLOAT16: "F16", DType.BFLOAT16: "BF16",
+    DType.FLOAT8_E4M3: "F8E4M3", DType.FLOAT8_E5M2: "F8E5M2", DType.INT64: "I64", DType.INT32: "I32",
+    DType.INT16: "I16", DType.INT8: "I8", DType.INT4: "I4", DType.UINT64: "U64", DType.UINT32: "U32",
+    DType.UINT16: "U16", DType.UINT8: "U8", DType.BOOL: "BOOL", DType.COMPLEX64: "C64", DType.COMPLEX128: "C128",
+    DType.INVALID: "INVALID",
+}
+
+_PARSE = {
+    DType.FLOAT64: ("F64", "FLOAT64", "DOUBLE"), DType.FLOAT32: ("F32", "FLOAT32", "FLOAT", "SINGLE"),
+    DType.FLOAT16: ("F16", "FLOAT16", "HALF"), DType.BFLOAT16: ("BF16", "BFLOAT16", "BRAINFLOAT16"),
+    DType.FLOAT8_E4M3: ("F8E4M3", "FP8E4M3", "FLOAT8E4M3"), DType.FLOAT8_E5M2: ("F8E5M2", "FP8E5M2", "FLOAT8E5M2"),
+    DType.INT64: ("I64", "INT64", "LONG"), DType.INT32: ("I32", "INT32", "INT"), DType.INT16: ("I16", "INT16", "SHORT"),
+    DType.INT8: ("I8", "INT8", "BYTE"), DType.INT4: ("I4", "INT4"), DType.UINT64: ("U64", "UINT64", "ULONG"),
+    DType.UINT32: ("U32", "UINT32", "UINT"), DType.UINT16: ("U16", "UINT16", "USHORT"),
+    DType.UINT8: ("U8", "UINT8", "UBYTE"), DType.BOOL: ("BOOL", "BOOLEAN", "B1"),
+    DType.COMPLEX64: ("C64", "COMPLEX64"), DType.COMPLEX128: ("C128", "COMPLEX128"),
 }
 
 # Formats the conversion kernels encode to (dtype/convert/convert.go:148-228)

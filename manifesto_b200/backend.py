@@ -326,6 +326,43 @@ class CUDABackend:
     def upload_sparse(self, *args, **kwargs):
         raise LayoutUnsupported("tensor: layout not supported")
 
+    def zeros(self, shape: Sequence[int], dtype: DType, stream=None) -> DeviceTensor:
+        """Upload(shape, dtype, make([]byte, n)) without the host buffer: a device memset."""
+        self._check()
+        t = self.empty(shape, dtype)
+        t._buffer.memset(0, stream)
+        if stream is None:
+            call("mf_stream_sync", None)
+        return t
+
+    def upload_float32_as(self, shape: Sequence[int], dtype: DType, values, stream=None) -> DeviceTensor:
+        """Upload(shape, dtype, Float32AsDTypeBytes(values, dtype)) with the encode on the device.
+
+        Float32AsDTypeBytes (runtime/session.go:431-452) encodes BF16 and F16 and
+        passes every other dtype through as float32 bytes; here the float32 values
+        cross PCIe once and mf_convert encodes them with the same rounding.  Like
+        the reference, a dtype that is none of F32/BF16/F16 gets float32 bytes and
+        so fails Upload's byte-count check (ShapeMismatch)."""
+        self._check()
+        dtype = DType(dtype)
+        vals = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+        if dtype not in (DType.FLOAT32, DType.BFLOAT16, DType.FLOAT16):
+            want = dtype.bytes_for(_shape_elements(shape))
+            raise ShapeMismatch(f"tensor: shape {tuple(shape)} x {dtype.name} needs {want} bytes, got {vals.nbytes}")
+        if vals.size != _shape_elements(shape):
+            raise ShapeMismatch(f"tensor: shape {tuple(shape)} x {dtype.name} needs "
+                                f"{dtype.bytes_for(_shape_elements(shape))} bytes, got "
+                                f"{dtype.bytes_for(vals.size)}")
+        if dtype == DType.FLOAT32:
+            return self.upload(shape, dtype, vals)
+        staged = self.upload(shape, DType.FLOAT32, vals)
+        try:
+            out = self.convert(staged, dtype, stream=stream)
+            call("mf_stream_sync", stream_handle(stream))  # the staging copy is freed next
+        finally:
+            staged.close()
+        return out
+
     def download(self, t: DeviceTensor) -> tuple[DType, bytes]:
         """Materialise a fresh host copy owned by the caller."""
         self._check()

@@ -18,8 +18,16 @@ that on the device for the two node kinds this path owns:
 
 Every other op is refused with MFError (MF_ERR_INVALID_ARGUMENT).  Values are device
 tensors keyed by graph input name or node ID; ``Graph.outputs`` maps output names to
-node IDs.  Nodes run in list order (the lowered graph is topologically sorted) on one
-stream; intermediate tensors no output refers to are freed when the call returns.
+node IDs.  Nodes run in list order (the lowered graph is topologically sorted);
+intermediate tensors no output refers to are freed when the call returns.
+
+Multi-stream execution: given a stream schedule (ir.ScheduleStreams output,
+ir/stream_scheduler.go:56-141 -- each node's StreamID and SyncBarriers), every
+StreamID maps to a CUDA stream and every EventID to a CUDA event, both resolved into
+flat tables before the first dispatch; a node waits (cudaStreamWaitEvent) on its Wait
+barriers, runs on its stream, then records (cudaEventRecord) its signal barriers.
+schedule_streams restates the scheduler over this module's Graph (edges are input
+names produced by earlier nodes) so a schedule can be made without the Go compiler.
 """
 from __future__ import annotations
 
@@ -70,6 +78,72 @@ class GraphCallResult:
     outputs: dict[str, DeviceTensor]
 
 
+@dataclass(frozen=True)
+class SyncEvent:
+    """ir.SyncEvent (ir/sync_event.go:14-26): wait before / signal after a node's dispatch."""
+    event_id: int
+    stream_id: int
+    wait: bool
+
+
+@dataclass
+class NodeSchedule:
+    """The scheduler's per-node output: ir.Node.StreamID and SyncBarriers (ir/node.go:43-51)."""
+    stream_id: int = 0
+    barriers: list[SyncEvent] = field(default_factory=list)
+
+
+def schedule_streams(g: "Graph", max_streams: int = 0) -> dict[str, NodeSchedule]:
+    """ir.ScheduleStreams (ir/stream_scheduler.go:56-141) and its pickStream rule (:229-287)
+    over a Graph: a node continues its single predecessor stream when it is the next node
+    of that stream's chain, a merge takes the lowest predecessor stream, anything else
+    opens a new stream while fewer than max_streams exist (<= 0: one per node).  A
+    predecessor on another stream gives the node a Wait barrier and the predecessor a
+    signal with the same event ID."""
+    cap = max_streams if max_streams >= 1 else len(g.nodes)
+    producer = {}
+    for i, n in enumerate(g.nodes):
+        producer.setdefault(n.id, i)
+    ids = {n.id: i + 1 for i, n in enumerate(g.nodes)}   # node.ID = index + 1
+    out = {n.id: NodeSchedule() for n in g.nodes}
+    last_on_stream: dict[int, int] = {}
+    next_stream, next_event = 0, 1
+    for i, n in enumerate(g.nodes):
+        preds: dict[int, int] = {}   # stream -> most recent producer node ID
+        for ref in n.inputs:
+            j = producer.get(ref)
+            if j is None or j >= i:
+                continue
+            p = g.nodes[j]
+            st = out[p.id].stream_id
+            if st not in preds or ids[p.id] > preds[st]:
+                preds[st] = ids[p.id]
+        if not preds:
+            if next_stream < cap:
+                assigned, next_stream = next_stream, next_stream + 1
+            else:
+                assigned = 0
+        elif len(preds) == 1:
+            (only, pred_id), = preds.items()
+            if last_on_stream.get(only) == pred_id:
+                assigned = only
+            elif next_stream < cap:
+                assigned, next_stream = next_stream, next_stream + 1
+            else:
+                assigned = only
+        else:
+            assigned = min(preds)
+        out[n.id].stream_id = assigned
+        last_on_stream[assigned] = ids[n.id]
+        for st, pred_id in preds.items():
+            if st == assigned:
+                continue
+            out[n.id].barriers.append(SyncEvent(next_event, st, True))
+            out[g.nodes[pred_id - 1].id].barriers.append(SyncEvent(next_event, st, False))
+            next_event += 1
+    return out
+
+
 class KernelSet:
     """codegen.KernelSet (codegen/attach.go:14-60): emitted kernels keyed by target."""
 
@@ -112,7 +186,53 @@ class GraphBackend:
         self.backend = backend
         self.compat = compat
 
-    def call_graph(self, request: GraphCallRequest, stream=None) -> GraphCallResult:
+    def call_graph(self, request: GraphCallRequest, stream=None,
+                   schedule: dict[str, NodeSchedule] | None = None) -> GraphCallResult:
+        """Run the graph on `stream`, or on the streams of `schedule` (see the module text).
+        With a schedule the call returns after every stream has finished."""
+        if schedule is None:
+            return self._call(request, lambda node: stream, None)
+        from .backend import Event, Stream
+        nodes = request.graph.nodes
+        for n in nodes:
+            if n.id not in schedule:
+                raise InvalidArgument(f"graph.call {request.graph_name!r}: node {n.id!r} has no stream assignment")
+        # flat handle tables, resolved before the first dispatch
+        stream_ids = sorted({schedule[n.id].stream_id for n in nodes} |
+                            {b.stream_id for n in nodes for b in schedule[n.id].barriers})
+        streams = {sid: Stream() for sid in stream_ids}
+        events = {b.event_id: Event() for n in nodes for b in schedule[n.id].barriers}
+        start = Event()
+        try:
+            # work already queued for the inputs on the caller's stream (the legacy
+            # default stream when none is given) comes first
+            start.record(stream)
+            for st in streams.values():
+                st.wait(start)
+
+            def on_stream(node: GraphNode):
+                sched = schedule[node.id]
+                for b in sched.barriers:
+                    if b.wait:
+                        streams[sched.stream_id].wait(events[b.event_id])
+                return streams[sched.stream_id]
+
+            def after(node: GraphNode) -> None:
+                for b in schedule[node.id].barriers:
+                    if not b.wait:
+                        events[b.event_id].record(streams[b.stream_id])
+
+            return self._call(request, on_stream, after, sync=list(streams.values()))
+        finally:
+            for st in streams.values():
+                st.sync()
+            for ev in events.values():
+                ev.close()
+            for st in streams.values():
+                st.close()
+            start.close()
+
+    def _call(self, request: GraphCallRequest, stream_for, after, sync=()) -> GraphCallResult:
         g = request.graph
         values: dict[str, DeviceTensor] = {}
         for name in g.inputs:
@@ -128,7 +248,9 @@ class GraphBackend:
                         raise InvalidArgument(f"graph.call {request.graph_name!r}: node {node.id!r} reads "
                                               f"unknown value {ref!r}")
                     args.append(values[ref])
-                out = self._run_node(node, args, stream)
+                out = self._run_node(node, args, stream_for(node))
+                if after is not None:
+                    after(node)
                 if out is not None and all(out is not a for a in args):
                     produced.append(out)
                 values[node.id] = out
@@ -139,9 +261,13 @@ class GraphBackend:
                                           f"unknown node {ref!r}")
                 outputs[name] = values[ref]
         except BaseException:
+            for st in sync:
+                st.sync()
             for t in produced:
                 t.close()
             raise
+        for st in sync:
+            st.sync()  # intermediates may still be in use on another stream
         keep = {id(t) for t in outputs.values()}
         for t in produced:
             if id(t) not in keep:

@@ -53,3 +53,38 @@ def test_graph_call_casts_and_fusion(backend, ref):
     for t in list(ins.values()) + list(out.values()):
         t.close()
     k.close()
+
+
+def test_scheduled_streams_match_serial(backend, ref):
+    """A diamond plus an independent branch, run on the streams schedule_streams assigns
+    (events between them), gives the same bytes as the serial run and as the oracle."""
+    n = 1 << 20
+    x = synthetic.normal_bf16(401, n)
+    y = synthetic.normal_bf16(402, n, 0.0, 30.0)
+    add = fusion.FusionAST(fusion.binary(fusion.NodeType.ADD, fusion.input_node(0), fusion.input_node(1)),
+                           ["b", "c"], "d", dtype=DType.FLOAT32)
+    k = fusion.emit_cuda(add, in_dtypes=[DType.FLOAT16, DType.BFLOAT16], out_dtype=DType.FLOAT32)
+    g = graph.Graph(nodes=[
+        graph.GraphNode("a", graph.SHAPE_CAST, ["x"], {"dtype": "F32"}),
+        graph.GraphNode("b", graph.SHAPE_CAST, ["a"], {"dtype": "F16"}),
+        graph.GraphNode("c", graph.SHAPE_CAST, ["a"], {"dtype": "BF16"}),
+        graph.GraphNode("d", graph.FUSE_OP, ["b", "c"], {graph.KERNEL_ATTRIBUTE: graph.KernelSet([k])}),
+        graph.GraphNode("e", graph.SHAPE_CAST, ["y"], {"dtype": "F8_E4M3"}),
+    ], inputs=["x", "y"], outputs={"d": "d", "e": "e"})
+    sched = graph.schedule_streams(g)
+    assert [sched[i].stream_id for i in "abcde"] == [0, 0, 1, 0, 2]
+    ins = {"x": backend.upload([n], DType.BFLOAT16, x), "y": backend.upload([n], DType.BFLOAT16, y)}
+    gb = graph.GraphBackend(backend)
+    par = gb.call_graph(graph.GraphCallRequest("diamond", g, ins), schedule=sched).outputs
+    ser = gb.call_graph(graph.GraphCallRequest("diamond", g, ins)).outputs
+    for name in ("d", "e"):
+        assert backend.download(par[name])[1] == backend.download(ser[name])[1]
+    a = ref.convert(x, BF16, F32)
+    b = ref.convert(a, F32, F16).view(np.uint16)
+    c = ref.convert(a, F32, BF16).view(np.uint16)
+    want_d = ref.fused_eval(fusion.node_table(add.root), [b, c], [F16, BF16], [0, 0], F32, n, threads=host_threads())
+    assert backend.download(par["d"])[1] == want_d.tobytes()
+    assert backend.download(par["e"])[1] == ref.convert(y, BF16, E4M3).tobytes()
+    for t in list(ins.values()) + list(par.values()) + list(ser.values()):
+        t.close()
+    k.close()

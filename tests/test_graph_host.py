@@ -125,3 +125,38 @@ def test_kernel_set():
     k = K()
     ks = graph.KernelSet([k])
     assert ks.for_target(Target.CUDA) is k and ks.for_target(Target.CPU) is None and ks.targets() == [Target.CUDA]
+
+
+def g_of(*nodes, outputs=None):
+    return graph.Graph([graph.GraphNode(i, graph.SHAPE_CAST, list(ins), {}) for i, ins in nodes], ["x", "y"],
+                       outputs or {})
+
+
+def sched(g, cap=0):
+    s = graph.schedule_streams(g, cap)
+    return {k: (v.stream_id, [(b.event_id, b.stream_id, b.wait) for b in v.barriers]) for k, v in s.items()}
+
+
+def test_schedule_chain_stays_on_one_stream():
+    assert sched(g_of(("a", "x"), ("b", "a"), ("c", "b"))) == {"a": (0, []), "b": (0, []), "c": (0, [])}
+
+
+def test_schedule_fork_and_merge():
+    # two roots open streams 0 and 1; the merge takes the lowest and waits on the other
+    got = sched(g_of(("a", "x"), ("b", "y"), ("c", ("a", "b"))))
+    assert got == {"a": (0, []), "b": (1, [(1, 1, False)]), "c": (0, [(1, 1, True)])}
+
+
+def test_schedule_diamond():
+    # b continues a's chain; c (also fed by a) finds the chain taken and opens stream 1;
+    # d merges onto stream 0 and waits on c's signal
+    got = sched(g_of(("a", "x"), ("b", "a"), ("c", "a"), ("d", ("b", "c"))))
+    assert got == {"a": (0, [(1, 0, False)]), "b": (0, []), "c": (1, [(1, 0, True), (2, 1, False)]),
+                   "d": (0, [(2, 1, True)])}
+
+
+def test_schedule_stream_cap():
+    got = sched(g_of(("a", "x"), ("b", "a"), ("c", "a"), ("d", ("b", "c"))), cap=1)
+    assert all(v == (0, []) for v in got.values())
+    got = sched(g_of(("a", "x"), ("b", "y"), ("c", "x")), cap=2)
+    assert got == {"a": (0, []), "b": (1, []), "c": (0, [])}

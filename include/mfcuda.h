@@ -123,6 +123,15 @@ int mf_last_error_copy(char* buf, size_t n);
  * with a code in *device_code). Synchronises the device. Backs
  * tensor.Tensor.Sync (tensor/tensor.go:53-130). */
 int mf_device_status(int* device_code);
+/* Device status code of a bounded wait that gave up (a bulk-copy stage that
+ * never landed, or mf_wait_flag's flag that was never set). */
+#define MF_DEVICE_TIMEOUT 0x7100
+/* Make `stream` wait until the int at device address `flag` equals `expect`
+ * (acquire load, polled with a short sleep), for at most `max_polls` polls;
+ * if it never does, record MF_DEVICE_TIMEOUT in the sticky status and let the
+ * stream continue. The building block for a handshake with a peer rank or the
+ * host that must not hang the GPU. No counterpart in the reference. */
+int mf_wait_flag(const int* flag, int expect, int64_t max_polls, mf_stream stream);
 /* Device properties used to size launches. */
 int mf_device_info(int* sm_count, int* cc_major, int* cc_minor, size_t* total_bytes);
 

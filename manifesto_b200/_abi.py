@@ -57,6 +57,7 @@ SIGNATURES: dict[str, list] = {
     "mf_shutdown": [],
     "mf_last_error_copy": [ctypes.c_char_p, _sz],
     "mf_device_status": [ctypes.POINTER(_int)],
+    "mf_wait_flag": [_vp, _int, _i64, _vp],
     "mf_device_info": [ctypes.POINTER(_int), ctypes.POINTER(_int), ctypes.POINTER(_int), ctypes.POINTER(_sz)],
     "mf_alloc": [ctypes.POINTER(_vp), _sz],
     "mf_free": [_vp],

@@ -35,7 +35,7 @@ constexpr int kConsumerWarps = kStreamThreads / 32;
 constexpr int64_t kTileElems = 8192;            // elements per tile
 constexpr int kStreamSmemBudget = 64 * 1024;    // staging bytes per CTA (3 CTAs per SM)
 constexpr uint32_t kMbarSpinLimit = 1u << 24;   // polls of try_wait before giving up
-constexpr int kDeviceTimeout = 0x7100;          // sticky status code of a timed-out wait
+constexpr int kDeviceTimeout = MF_DEVICE_TIMEOUT;  // sticky status code of a timed-out wait
 
 struct ChunkRec {
     const void* src;

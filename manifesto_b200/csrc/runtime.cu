@@ -63,6 +63,19 @@ int64_t stream_grid(int64_t work_items, int threads, int blocks_per_sm) {
     return blocks;
 }
 
+// One thread polls the flag with acquire loads, sleeping between polls; when
+// the poll budget runs out it records MF_DEVICE_TIMEOUT and returns, so the
+// stream moves on and the context stays usable.
+__global__ void wait_flag_kernel(const int* flag, int expect, int64_t max_polls, int* status) {
+    for (int64_t i = 0; i < max_polls; ++i) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if (v == expect) return;
+        __nanosleep(256);
+    }
+    atomicExch(status, MF_DEVICE_TIMEOUT);
+}
+
 }  // namespace mf
 
 using namespace mf;
@@ -139,6 +152,19 @@ int mf_device_status(int* device_code) {
         MF_CUDA_CHECK(cudaMemcpyToSymbol(g_sticky_status, &zero, sizeof(int)));
         return fail(MF_ERR_DEVICE_STICKY, "mfcuda: a kernel recorded device status %d", code);
     }
+    return MF_OK;
+}
+
+int mf_wait_flag(const int* flag, int expect, int64_t max_polls, mf_stream stream) {
+    MF_ENTER();
+    if (!flag) return fail(MF_ERR_INVALID_ARGUMENT, "mf_wait_flag: flag is NULL");
+    if (reinterpret_cast<uintptr_t>(flag) % alignof(int))
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_wait_flag: flag is not 4-byte aligned");
+    if (max_polls < 0) return fail(MF_ERR_INVALID_ARGUMENT, "mf_wait_flag: negative poll budget");
+    int* status = sticky_status_ptr();
+    if (!status) return fail(MF_ERR_CUDA, "mf_wait_flag: sticky status word unavailable");
+    wait_flag_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(flag, expect, max_polls, status);
+    MF_LAUNCH_CHECK("mf_wait_flag");
     return MF_OK;
 }
 

@@ -127,59 +127,90 @@ def quantise(chunks: ctypes.Array, n_chunks: int, n_tensors: int, d_amax: int, d
 class StreamedQuantiser:
     """Quantise checkpoints that live in (pinned) host memory, one after another.
 
-    A checkpoint shard is uploaded, quantised and downloaded in a pipeline of
-    three CUDA streams -- upload, compute, download -- over two device slots,
-    so the FP8 download of checkpoint i runs on the PCIe link while the BF16
-    upload of checkpoint i+1 runs in the other direction, and the kernels run
-    between them.  ``submit`` returns as soon as the work is queued.
+    A checkpoint shard streams through the device in batches of whole tensors: each
+    batch is uploaded, quantised (its tensors' amax, the all-reduce when there is a
+    communicator, the cast) and downloaded on three CUDA streams -- upload, compute,
+    download -- over two device slots, so a batch's FP8 download runs on the PCIe link
+    while the next batch's BF16 upload runs in the other direction, and only the last
+    batch's download is left when the last upload ends.  Per-tensor scaling needs a
+    whole tensor, never a whole checkpoint, so batching changes no result.
+    ``submit`` returns as soon as the work is queued.
 
-    sizes[t] is this rank's element count of tensor t (its row range); the
-    host buffers hold the shards back to back in tensor order: BF16 source
-    (2 bytes per element), FP8 destination (1 byte per element) and the
-    float32 scale_inv vector.
+    sizes[t] is this rank's element count of tensor t (its row range); the host
+    buffers hold the shards back to back in tensor order: source (2 bytes per element
+    for BF16/F16, 4 for F32), FP8 destination (1 byte per element) and the float32
+    scale_inv vector.  Tensors are cut into batches of at most ``batch_bytes`` of
+    source by ``batch_sizes`` (default: sizes); with a communicator every rank must
+    pass the same batch_sizes (the global tensor sizes, say), because each batch is one
+    all-reduce.
     """
 
     def __init__(self, sizes: Sequence[int], fp8_dtype: DType = DType.FLOAT8_E4M3, compat: int = 0,
-                 comm: Communicator | None = None, src_dtype: DType = DType.BFLOAT16):
+                 comm: Communicator | None = None, src_dtype: DType = DType.BFLOAT16, batch_bytes: int = 1 << 30,
+                 batch_sizes: Sequence[int] | None = None):
         from .backend import DeviceBuffer, Event, Stream
         self.sizes = [int(s) for s in sizes]
         self.n_tensors = len(self.sizes)
         self.total = sum(self.sizes)
         self.esize = 2 if src_dtype in (DType.BFLOAT16, DType.FLOAT16) else 4
         self.src_dtype, self.fp8_dtype, self.compat, self.comm = src_dtype, fp8_dtype, compat, comm
+        key = [int(s) for s in (batch_sizes if batch_sizes is not None else sizes)]
+        if len(key) != self.n_tensors:
+            raise ValueError(f"StreamedQuantiser: {len(key)} batch sizes for {self.n_tensors} tensors")
+        # batches: consecutive tensor ranges [t0, t1)
+        self.batches: list[tuple[int, int]] = []
+        t0, acc = 0, 0
+        for t in range(self.n_tensors):
+            b = self.esize * key[t]
+            if t > t0 and acc + b > batch_bytes:
+                self.batches.append((t0, t))
+                t0, acc = t, 0
+            acc += b
+        if self.n_tensors:
+            self.batches.append((t0, self.n_tensors))
+        self.offsets = [0]
+        for n in self.sizes:
+            self.offsets.append(self.offsets[-1] + n)
+        slot_elems = max([self.offsets[b] - self.offsets[a] for a, b in self.batches] or [0])
+        slot_t = max([b - a for a, b in self.batches] or [1])
         self.up, self.compute, self.down = Stream(), Stream(), Stream()
         self.slots = []
         for _ in range(2):
-            src = DeviceBuffer(max(1, self.esize * self.total))
-            dst = DeviceBuffer(max(1, self.total))
-            amax = DeviceBuffer(4 * self.n_tensors)
-            sinv = DeviceBuffer(4 * self.n_tensors)
-            entries, off = [], 0
-            for t, n in enumerate(self.sizes):
-                entries.append((src.ptr + self.esize * off, dst.ptr + off, n, t, src_dtype))
-                off += n
-            self.slots.append({"src": src, "dst": dst, "amax": amax, "sinv": sinv,
-                               "chunks": make_chunks(entries), "uploaded": Event(), "computed": Event(),
-                               "downloaded": Event(), "used": False})
+            src = DeviceBuffer(max(1, self.esize * slot_elems))
+            dst = DeviceBuffer(max(1, slot_elems))
+            amax = DeviceBuffer(4 * slot_t)
+            sinv = DeviceBuffer(4 * slot_t)
+            chunks = []
+            for a, b in self.batches:
+                entries, off = [], 0
+                for t in range(a, b):
+                    entries.append((src.ptr + self.esize * off, dst.ptr + off, self.sizes[t], t - a, src_dtype))
+                    off += self.sizes[t]
+                chunks.append(make_chunks(entries))
+            self.slots.append({"src": src, "dst": dst, "amax": amax, "sinv": sinv, "chunks": chunks,
+                               "uploaded": Event(), "computed": Event(), "downloaded": Event(), "used": False})
         self.count = 0
 
     def submit(self, host_src: int, host_dst: int, host_scale_inv: int) -> None:
         """Queue one checkpoint: host_src -> device -> quantise -> host_dst, host_scale_inv."""
-        s = self.slots[self.count % 2]
-        if s["used"]:
-            self.up.wait(s["downloaded"])  # the slot's previous results have left the device
-        call("mf_memcpy_h2d_async", s["src"].ptr, int(host_src), self.esize * self.total, self.up.handle)
-        s["uploaded"].record(self.up)
-        self.compute.wait(s["uploaded"])
-        quantise(s["chunks"], self.n_tensors, self.n_tensors, s["amax"].ptr, s["sinv"].ptr, self.fp8_dtype,
-                 self.compat, self.comm, self.compute)
-        s["computed"].record(self.compute)
-        self.down.wait(s["computed"])
-        call("mf_memcpy_d2h_async", int(host_dst), s["dst"].ptr, self.total, self.down.handle)
-        call("mf_memcpy_d2h_async", int(host_scale_inv), s["sinv"].ptr, 4 * self.n_tensors, self.down.handle)
-        s["downloaded"].record(self.down)
-        s["used"] = True
-        self.count += 1
+        for bi, (a, b) in enumerate(self.batches):
+            s = self.slots[self.count % 2]
+            if s["used"]:
+                self.up.wait(s["downloaded"])  # the slot's previous results have left the device
+            e0, e1 = self.offsets[a], self.offsets[b]
+            call("mf_memcpy_h2d_async", s["src"].ptr, int(host_src) + self.esize * e0, self.esize * (e1 - e0),
+                 self.up.handle)
+            s["uploaded"].record(self.up)
+            self.compute.wait(s["uploaded"])
+            quantise(s["chunks"][bi], b - a, b - a, s["amax"].ptr, s["sinv"].ptr, self.fp8_dtype, self.compat,
+                     self.comm, self.compute)
+            s["computed"].record(self.compute)
+            self.down.wait(s["computed"])
+            call("mf_memcpy_d2h_async", int(host_dst) + e0, s["dst"].ptr, e1 - e0, self.down.handle)
+            call("mf_memcpy_d2h_async", int(host_scale_inv) + 4 * a, s["sinv"].ptr, 4 * (b - a), self.down.handle)
+            s["downloaded"].record(self.down)
+            s["used"] = True
+            self.count += 1
 
     def synchronize(self) -> None:
         for st in (self.up, self.compute, self.down):

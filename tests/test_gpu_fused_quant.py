@@ -370,13 +370,18 @@ def test_ckpt_many_chunks_and_ragged(backend, ref):
         b.free()
 
 
-def test_streamed_quantiser_host_checkpoints(backend, ref):
-    """Three host-resident checkpoints through the upload/compute/download pipeline (two slots)."""
+@pytest.mark.parametrize("batch_bytes", [1 << 30, 300_000])
+def test_streamed_quantiser_host_checkpoints(backend, ref, batch_bytes):
+    """Three host-resident checkpoints through the upload/compute/download pipeline (two slots):
+    one batch per checkpoint, or many batches of whole tensors (a tensor larger than the batch
+    gets one of its own)."""
     from manifesto_b200 import PinnedBuffer
     specs = small_layout()
     sizes = [s.numel for s in specs]
     total = sum(sizes)
-    q = checkpoint.StreamedQuantiser(sizes)
+    q = checkpoint.StreamedQuantiser(sizes, batch_bytes=batch_bytes)
+    assert (len(q.batches) == 1) == (batch_bytes == 1 << 30)
+    assert [t for a, b in q.batches for t in range(a, b)] == list(range(len(sizes)))
     ins, outs, sis, hosts = [], [], [], []
     for k in range(3):
         host = [synthetic.normal_bf16(4000 + 100 * k + i, n, 0.0, 0.02 * (k + 1)) for i, n in enumerate(sizes)]

@@ -14,8 +14,7 @@
 //     the scale index a shift of the word index;
 //   * row words (cols % 8 == 0, group % 8 == 0): the same per-word body on a
 //     (row segment, row) grid;
-//   * 32-element chunks (cols % 32 == 0, group % 32 == 0) and a per-element
-//     kernel for any even cols.
+//   * a per-element kernel for any even cols.
 // Lane l of a warp owns word w0 + l: a warp reads 128 contiguous bytes of q
 // and writes 512 contiguous bytes of BF16.  Nibble -> float uses the exponent
 // trick: (n ^ 8) | 0x4B000000 is the float 2^23 + q + 8, so q = that -
@@ -28,7 +27,6 @@ namespace mf {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kElems = 32;  // elements per thread-chunk (16 packed bytes)
 
 template <int SDT>
 __device__ __forceinline__ float load_scale(const void* s, int64_t i) {
@@ -41,48 +39,6 @@ __device__ __forceinline__ float load_scale(const void* s, int64_t i) {
 __device__ __forceinline__ float nibble_f32(uint32_t w, int k) {
     const uint32_t bits = ((w >> (4 * k)) & 0xfu) ^ 0x4B000008u;
     return __fsub_rn(__uint_as_float(bits), 8388616.0f);
-}
-
-template <int SDT, int ODT>
-__global__ void __launch_bounds__(kThreads) int4_dequant_vec_kernel(const uint4* __restrict__ q,
-                                                                   const void* __restrict__ scales,
-                                                                   void* __restrict__ out, int64_t nchunks,
-                                                                   uint32_t chunks_per_row,
-                                                                   uint32_t chunks_per_group,
-                                                                   int64_t ngroups) {
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nchunks; c += stride) {
-        const uint4 packed = ld_stream(q + c);
-        const int64_t row = c / chunks_per_row;
-        const uint32_t cr = static_cast<uint32_t>(c - row * chunks_per_row);
-        const float s = load_scale<SDT>(scales, row * ngroups + cr / chunks_per_group);
-        const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
-        float v[kElems];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) v[8 * j + k] = x86_mul(nibble_f32(w[j], k), s);
-        }
-        if constexpr (ODT == MF_DT_F32) {
-            uint4* o = reinterpret_cast<uint4*>(out) + c * 8;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                st_stream(o + j, make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
-                                            __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3])));
-        } else {
-            uint4* o = reinterpret_cast<uint4*>(out) + c * 4;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                uint32_t p[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float lo = v[8 * j + 2 * k], hi = v[8 * j + 2 * k + 1];
-                    p[k] = (ODT == MF_DT_BF16) ? f32x2_to_bf16x2(lo, hi) : f32x2_to_f16x2(lo, hi);
-                }
-                st_stream(o + j, make_uint4(p[0], p[1], p[2], p[3]));
-            }
-        }
-    }
 }
 
 // One packed word (8 nibbles, elements e .. e+7) times its group scale,
@@ -225,8 +181,6 @@ int launch(const void* q, const void* scales, void* out, int64_t rows, int64_t c
     const int64_t ngroups = (cols + group - 1) / group;
     const bool words = (cols % 8 == 0) && (group % 8 == 0) && aligned16(q) && aligned16(out) &&
                        (cols / 8) < (int64_t(1) << 31);
-    const bool vec = (cols % kElems == 0) && (group % kElems == 0) && aligned16(q) && aligned16(out) &&
-                     (cols / kElems) < (int64_t(1) << 31);
     if (words) {
         const uint32_t words_per_row = static_cast<uint32_t>(cols / 8);
         const uint32_t group_words = static_cast<uint32_t>(group / 8);
@@ -248,12 +202,6 @@ int launch(const void* q, const void* scales, void* out, int64_t rows, int64_t c
             int4_dequant_words_kernel<SDT, ODT><<<grid, kThreads, 0, s>>>(
                 static_cast<const uint32_t*>(q), scales, out, rows, words_per_row, gw_shift, group_words, ngroups);
         }
-    } else if (vec) {
-        const int64_t nchunks = rows * cols / kElems;
-        const int64_t blocks = stream_grid(nchunks, kThreads, 8);
-        int4_dequant_vec_kernel<SDT, ODT><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
-            static_cast<const uint4*>(q), scales, out, nchunks, static_cast<uint32_t>(cols / kElems),
-            static_cast<uint32_t>(group / kElems), ngroups);
     } else {
         const int64_t blocks = stream_grid(rows * cols, kThreads, 8);
         int4_dequant_scalar_kernel<SDT, ODT><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(

@@ -157,6 +157,21 @@ def test_swiglu_specialised_within_1ulp(backend, ref):
     assert amax == float(np.abs((got.astype(np.uint32) << 16).view(np.float32)).max())
 
 
+def test_swiglu_row_length_without_stationary_grid(backend, ref):
+    """A row of 8191 vectors (prime) admits no grid holding a multiple of the row in threads:
+    the kernel that advances the row index per step runs, with the same results."""
+    hidden = 8 * 8191
+    n = hidden * 5
+    f, k = swiglu_kernel(hidden)
+    assert k.specialised()
+    ins = swiglu_inputs(n, hidden=hidden, seed=77)
+    got, amax = run_fused(k, ins, n, BF16, amax=True)
+    want = ref.fused_eval(fusion.node_table(f.root), ins, [BF16] * 4, [0, hidden, hidden, 0], BF16, n,
+                          threads=host_threads())
+    assert ulp_diff_16(got, want).max() <= 1
+    assert amax == float(np.abs((got.astype(np.uint32) << 16).view(np.float32)).max())
+
+
 def test_swiglu_specialised_extreme_inputs(backend, ref):
     """t = x*g + b swept through the range where e^-t leaves float32 (t < -88.7) and
     1/(1 + e^-t) turns subnormal, plus Inf, NaN, zeros and subnormal inputs: the fast

@@ -199,20 +199,6 @@ __device__ __forceinline__ float x86_fma(float a, float b, float c) {
     return __uint_as_float(0xffc00000u);
 }
 
-// ------------------------------------------------- approximate math
-
-// 2^x and 1/x on the SFU (PTX ex2.approx.f32 / rcp.approx.f32, subnormals kept).
-__device__ __forceinline__ float exp2f_approx(float x) {
-    float r;
-    asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-__device__ __forceinline__ float rcp_approx(float x) {
-    float r;
-    asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-
 // ----------------------------------------------------- float64 -> f32
 
 // float32(float64) as the amd64 Go conversion does it: RNE, and a NaN

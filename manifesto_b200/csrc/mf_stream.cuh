@@ -110,19 +110,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
-template <int Bytes>
-__device__ __forceinline__ void load_raw_smem(const uint8_t* tile, int c, RawChunk<Bytes>& r) {
-    const uint4* p = reinterpret_cast<const uint4*>(tile) + c * Bytes;
-#pragma unroll
-    for (int k = 0; k < Bytes; ++k) {
-        const uint4 v = p[k];
-        r.w[4 * k + 0] = v.x;
-        r.w[4 * k + 1] = v.y;
-        r.w[4 * k + 2] = v.z;
-        r.w[4 * k + 3] = v.w;
-    }
-}
-
 // ------------------------------------------------------------ lane steps
 //
 // In one step a lane owns kLane consecutive elements (4 or 8) and lane l of

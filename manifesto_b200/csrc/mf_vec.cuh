@@ -3,11 +3,10 @@
 // Two granularities:
 //   * chunks of 16 elements (16 B of an 8-bit format, 32 B of a 16-bit
 //     format, 64 B of float32) read with one to four 128-bit loads, used by
-//     kernels whose per-thread work is naturally 16 elements (the Int4
-//     dequant, the amax folds);
+//     the amax folds;
 //   * quads of 4 elements, owned by consecutive lanes so every warp-wide
 //     access is one contiguous span whatever the element widths, used by the
-//     element-wise maps (conversion, casts, axpy).
+//     element-wise maps (the streaming engine's lane steps, axpy).
 // Inputs are read with the non-coherent path and the evict-first hint (each
 // byte is read once); outputs are written with the streaming store hint.
 #pragma once
@@ -51,13 +50,6 @@ __device__ __forceinline__ void load_raw(const void* base, int64_t c, RawChunk<B
     }
 }
 
-template <int Bytes>
-__device__ __forceinline__ void store_raw(void* base, int64_t c, const RawChunk<Bytes>& r) {
-    uint4* p = reinterpret_cast<uint4*>(base) + c * Bytes;
-#pragma unroll
-    for (int k = 0; k < Bytes; ++k) st_stream(p + k, make_uint4(r.w[4 * k], r.w[4 * k + 1], r.w[4 * k + 2], r.w[4 * k + 3]));
-}
-
 // f16x2 bits -> two float32 (exact for every non-NaN value).
 __device__ __forceinline__ void f16x2_to_f32x2(uint32_t h2, float& lo, float& hi) {
     asm("{\n\t.reg .f16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
@@ -71,62 +63,6 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
     const uint16_t x = static_cast<uint16_t>(two);
     asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(x));
     return r;
-}
-
-// Decode 16 elements of a floating storage format to float32.
-// E4M3, E5M2 and F16 widen through the hardware conversions (exact for
-// every non-NaN code); a word holding a NaN code is redone with the integer
-// codecs so NaN lanes get the reference's bit patterns
-// (sign | 0x7fc00000 [| payload]).  The NaN tests are SWAR on the packed codes.
-template <int DT>
-__device__ __forceinline__ void decode16(const RawChunk<dtype_bytes(DT)>& r, float (&v)[kChunk]) {
-    if constexpr (DT == MF_DT_F32) {
-#pragma unroll
-        for (int k = 0; k < kChunk; ++k) v[k] = __uint_as_float(r.w[k]);
-    } else if constexpr (DT == MF_DT_BF16) {
-#pragma unroll
-        for (int k = 0; k < kChunk; ++k) {
-            const uint32_t w = r.w[k >> 1];
-            v[k] = __uint_as_float((k & 1) ? (w & 0xffff0000u) : (w << 16));
-        }
-    } else if constexpr (DT == MF_DT_F16) {
-#pragma unroll
-        for (int k = 0; k < kChunk / 2; ++k) {
-            const uint32_t w = r.w[k];
-            f16x2_to_f32x2(w, v[2 * k], v[2 * k + 1]);
-            // half h is NaN iff (h & 0x7fff) + 0x3ff carries into bit 15
-            if (((w & 0x7fff7fffu) + 0x03ff03ffu) & 0x80008000u) {
-                v[2 * k] = __uint_as_float(f16_to_f32bits(w & 0xffffu));
-                v[2 * k + 1] = __uint_as_float(f16_to_f32bits(w >> 16));
-            }
-        }
-    } else if constexpr (DT == MF_DT_F8E4M3) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t w = r.w[k];
-            f16x2_to_f32x2(e4m3x2_to_f16x2(w), v[4 * k], v[4 * k + 1]);
-            f16x2_to_f32x2(e4m3x2_to_f16x2(w >> 16), v[4 * k + 2], v[4 * k + 3]);
-            // byte b is NaN iff (b & 0x7f) == 0x7f: zero byte of x = ~w & 0x7f7f7f7f
-            const uint32_t x = ~w & 0x7f7f7f7fu;
-            if ((x - 0x01010101u) & ~x & 0x80808080u) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) v[4 * k + j] = __uint_as_float(e4m3_to_f32bits((w >> (8 * j)) & 0xffu));
-            }
-        }
-    } else if constexpr (DT == MF_DT_F8E5M2) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t w = r.w[k];
-            // an E5M2 code is the high byte of the binary16 with the same value
-            f16x2_to_f32x2(__byte_perm(w, 0u, 0x1404u), v[4 * k], v[4 * k + 1]);
-            f16x2_to_f32x2(__byte_perm(w, 0u, 0x3424u), v[4 * k + 2], v[4 * k + 3]);
-            // byte b is NaN iff (b & 0x7f) > 0x7c, i.e. (b & 0x7f) + 3 sets bit 7
-            if (((w & 0x7f7f7f7fu) + 0x03030303u) & 0x80808080u) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) v[4 * k + j] = __uint_as_float(e5m2_to_f32bits((w >> (8 * j)) & 0xffu));
-            }
-        }
-    }
 }
 
 // Packed RNE conversions for inputs known not to be NaN (the hardware and the
@@ -347,23 +283,6 @@ __device__ __forceinline__ void encode4(const float (&v)[4], uint32_t* o, int co
 
 // Quad-sized vector access: 4 elements of `Bytes` each.
 template <int Bytes>
-__device__ __forceinline__ void load4(const void* p, uint32_t* w) {
-    if constexpr (Bytes == 1) {
-        w[0] = *static_cast<const uint32_t*>(p);
-    } else if constexpr (Bytes == 2) {
-        const uint2 x = *static_cast<const uint2*>(p);
-        w[0] = x.x;
-        w[1] = x.y;
-    } else {
-        const uint4 x = *static_cast<const uint4*>(p);
-        w[0] = x.x;
-        w[1] = x.y;
-        w[2] = x.z;
-        w[3] = x.w;
-    }
-}
-
-template <int Bytes>
 __device__ __forceinline__ void store4_stream(void* p, const uint32_t* w) {
     if constexpr (Bytes == 1) {
         asm volatile("st.global.cs.u32 [%0], %1;" ::"l"(p), "r"(w[0]) : "memory");
@@ -400,27 +319,6 @@ __device__ __forceinline__ void load4_stream(const void* p, uint32_t* w) {
         asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                      : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
                      : "l"(p));
-    }
-}
-
-// Encode 16 float32 values to a storage format.
-template <int DT>
-__device__ __forceinline__ void encode16(const float (&v)[kChunk], RawChunk<dtype_bytes(DT)>& r, int compat) {
-    if constexpr (DT == MF_DT_F32) {
-#pragma unroll
-        for (int k = 0; k < kChunk; ++k) r.w[k] = __float_as_uint(v[k]);
-    } else if constexpr (DT == MF_DT_BF16) {
-#pragma unroll
-        for (int k = 0; k < kChunk / 2; ++k) r.w[k] = f32x2_to_bf16x2(v[2 * k], v[2 * k + 1]);
-    } else if constexpr (DT == MF_DT_F16) {
-#pragma unroll
-        for (int k = 0; k < kChunk / 2; ++k) r.w[k] = f32x2_to_f16x2(v[2 * k], v[2 * k + 1]);
-    } else if constexpr (DT == MF_DT_F8E4M3 || DT == MF_DT_F8E5M2) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float q[4] = {v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]};
-            encode4<DT>(q, &r.w[k], compat);
-        }
     }
 }
 

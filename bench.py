@@ -515,8 +515,15 @@ def cpu_baseline(steps: int, warmup: int, tensors=None) -> dict:
     for _ in range(steps):
         cpu_step(tensors, threads)
     dt = (time.perf_counter() - t) / steps
+    # the Go loops are single-goroutine: one thread on one tensor of the sample, too
+    one = tensors[0]
+    t = time.perf_counter()
+    cpu_step([one], 1)
+    dt1 = time.perf_counter() - t
     return {"value": n / dt, "unit": "elems/s", "cores": threads, "kind": "port", "sample": CPU_SAMPLE,
-            "s_per_step": dt, "cpu": cpu_model()}
+            "s_per_step": dt, "cpu": cpu_model(),
+            "single_thread": {"value": one.size / dt1, "unit": "elems/s", "cores": 1,
+                              "sample": f"the first tensor of the sample ({one.size:,} params), one pass"}}
 
 
 def cpu_model() -> str:
@@ -544,7 +551,7 @@ def run_reference(args, world: int, rank: int) -> None:
                    "dst_dtype": "fp8e4m3", "compat": "reference", "sample": CPU_SAMPLE},
         "impl": "reference",
         "cpu_baseline": {"value": b["value"], "unit": "elems/s", "cores": b["cores"], "kind": "port",
-                         "sample": CPU_SAMPLE, "cpu": b["cpu"]},
+                         "sample": CPU_SAMPLE, "cpu": b["cpu"], "single_thread": b["single_thread"]},
         "e2e": {"value": b["value"], "unit": "elems/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "manifesto is Go and no Go toolchain exists here; this times the C restatement of its scalar "
                 "loops (oracle/mfref.c) with all host threads",

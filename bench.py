@@ -427,7 +427,7 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
                        "compat": "reference", "parallelism": f"rowsplit{world}",
                        "l2": "inputs larger than L2 (BF16 shard of 16.06 GB / N per rank)"},
             "hbm_gbs_job": round(job_gbs, 1), "alg_bytes_per_param": 5,
-            "roofline": roofline, "e2e": e2e, "clocks": clocks, "gpu_launches": 2 * args.steps,
+            "roofline": roofline, "e2e": e2e, "clocks": clocks, "gpu_launches": 3 * args.steps,
         }
         if kernels:
             line["kernels"] = kernels

@@ -49,7 +49,6 @@ struct ChunkRec {
 template <int MaxChunks>
 struct StreamArgs {
     const float* amax;   // per-tensor amax (cast ops)
-    float* scale_inv;    // per-tensor 1/scale output (cast ops), may be NULL
     int* status;         // sticky status word
     int64_t total_tiles;
     int32_t n_chunks;
@@ -258,8 +257,6 @@ struct ConvertOp {
     struct State {};
     template <class A>
     __device__ static State setup(const A&, const ChunkRec&) { return {}; }
-    template <class A>
-    __device__ static void first_tile(const A&, const ChunkRec&) {}
     template <bool DEFER>
     __device__ static void step(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State&, FixQueue& fq) {
         float v[2][4];
@@ -315,10 +312,6 @@ struct CastOp {
     template <class A>
     __device__ static State setup(const A& a, const ChunkRec& ch) {
         return {scale_from_amax(a.amax[ch.tensor], FP8)};
-    }
-    template <class A>
-    __device__ static void first_tile(const A& a, const ChunkRec& ch) {
-        if (a.scale_inv) a.scale_inv[ch.tensor] = scale_inv_from_amax(a.amax[ch.tensor], FP8);
     }
     template <bool DEFER>
     __device__ static void step(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State& st, FixQueue& fq) {
@@ -463,7 +456,6 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
             if (lane == 0) atomicExch(a.status, kDeviceTimeout);
             return;  // the producer's own bounded waits end the CTA
         }
-        if (tile == 0 && threadIdx.x == 0) Op::first_tile(a, ch);
         if (ch.aligned) {
             // lane-consecutive runs: every warp access is one contiguous span
             // only the first ((cnt * kIn) & ~15) bytes were copied (16-byte

@@ -191,6 +191,20 @@ __device__ __forceinline__ uint32_t encode_fp8(float v, int compat) {
     return encode_f32<FP8>(v, compat);
 }
 
+// scale_inv[t] = amax[t] / fp8_max (1 when amax is 0 or not finite) for every
+// tensor of the call, including a tensor this rank holds no element of.
+__global__ void scale_inv_kernel(const float* __restrict__ amax, float* __restrict__ scale_inv, int n, int fp8) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n) scale_inv[t] = scale_inv_from_amax(amax[t], fp8);
+}
+
+int launch_scale_inv(const float* d_amax, float* d_scale_inv, int n, int fp8_dtype, cudaStream_t s) {
+    if (!d_scale_inv || n <= 0) return MF_OK;
+    scale_inv_kernel<<<(n + 255) / 256, 256, 0, s>>>(d_amax, d_scale_inv, n, fp8_dtype);
+    MF_LAUNCH_CHECK("scale_inv launch");
+    return MF_OK;
+}
+
 template <int SRC>
 void amax_dispatch(const void* src, int64_t n, float* d_amax, cudaStream_t s) {
     if (aligned16(src)) {
@@ -203,21 +217,19 @@ void amax_dispatch(const void* src, int64_t n, float* d_amax, cudaStream_t s) {
 }
 
 template <int SRC, int FP8>
-cudaError_t cast_dispatch(const void* src, void* dst, int64_t n, const float* d_amax, float* d_scale_inv, int compat,
-                          cudaStream_t s) {
+cudaError_t cast_dispatch(const void* src, void* dst, int64_t n, const float* d_amax, int compat, cudaStream_t s) {
     StreamArgs<1> a{};
     single_chunk(a, src, dst, n, aligned16(src) && aligned16(dst));
     a.amax = d_amax;
-    a.scale_inv = d_scale_inv;
     if (compat) return launch_stream<CastOp<SRC, FP8, 1>, 1>(a, state().sm_count, s);
     return launch_stream<CastOp<SRC, FP8, 0>, 1>(a, state().sm_count, s);
 }
 
 template <int SRC>
-cudaError_t cast_dispatch_fp8(int fp8_dtype, const void* src, void* dst, int64_t n, const float* d_amax,
-                              float* d_scale_inv, int compat, cudaStream_t s) {
-    if (fp8_dtype == MF_DT_F8E4M3) return cast_dispatch<SRC, MF_DT_F8E4M3>(src, dst, n, d_amax, d_scale_inv, compat, s);
-    return cast_dispatch<SRC, MF_DT_F8E5M2>(src, dst, n, d_amax, d_scale_inv, compat, s);
+cudaError_t cast_dispatch_fp8(int fp8_dtype, const void* src, void* dst, int64_t n, const float* d_amax, int compat,
+                              cudaStream_t s) {
+    if (fp8_dtype == MF_DT_F8E4M3) return cast_dispatch<SRC, MF_DT_F8E4M3>(src, dst, n, d_amax, compat, s);
+    return cast_dispatch<SRC, MF_DT_F8E5M2>(src, dst, n, d_amax, compat, s);
 }
 
 // ----------------------------------------------------- grouped (ckpt)
@@ -378,12 +390,13 @@ int launch_amax(const void* src, int src_dtype, int64_t n, float* d_amax, cudaSt
 
 int launch_scaled_cast(const void* src, int src_dtype, void* dst, int fp8_dtype, const float* d_amax,
                        float* d_scale_inv, int64_t n, int compat, cudaStream_t s) {
-    if (n == 0) return MF_OK;
+    int rc = launch_scale_inv(d_amax, d_scale_inv, 1, fp8_dtype, s);
+    if (rc || n == 0) return rc;
     cudaError_t err;
     switch (src_dtype) {
-    case MF_DT_F32: err = cast_dispatch_fp8<MF_DT_F32>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
-    case MF_DT_F16: err = cast_dispatch_fp8<MF_DT_F16>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
-    case MF_DT_BF16: err = cast_dispatch_fp8<MF_DT_BF16>(fp8_dtype, src, dst, n, d_amax, d_scale_inv, compat, s); break;
+    case MF_DT_F32: err = cast_dispatch_fp8<MF_DT_F32>(fp8_dtype, src, dst, n, d_amax, compat, s); break;
+    case MF_DT_F16: err = cast_dispatch_fp8<MF_DT_F16>(fp8_dtype, src, dst, n, d_amax, compat, s); break;
+    case MF_DT_BF16: err = cast_dispatch_fp8<MF_DT_BF16>(fp8_dtype, src, dst, n, d_amax, compat, s); break;
     default: return fail(MF_ERR_DTYPE_UNSUPPORTED, "scaled cast: source dtype %d unsupported", src_dtype);
     }
     if (err != cudaSuccess) return cuda_fail(err, "scaled cast launch");
@@ -419,7 +432,6 @@ extern "C" int mf_fp8_scaled_cast(const void* src, int src_dtype, void* dst, int
     if (rc) return rc;
     if (!d_amax) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fp8_scaled_cast: d_amax is NULL");
     if (n > 0 && (!src || !dst)) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fp8_scaled_cast: NULL buffer");
-    if (n == 0) return MF_OK;
     return launch_scaled_cast(src, src_dtype, dst, fp8_dtype, d_amax, d_scale_inv, n, compat,
                               static_cast<cudaStream_t>(stream));
 }
@@ -433,7 +445,7 @@ extern "C" int mf_fp8_quantize(const void* src, int src_dtype, void* dst, int fp
     if (n > 0 && (!src || !dst)) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fp8_quantize: NULL buffer");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     MF_CUDA_CHECK(cudaMemsetAsync(d_amax, 0, sizeof(float), s));
-    if (n == 0) return MF_OK;
+    if (n == 0) return launch_scale_inv(d_amax, d_scale_inv, 1, fp8_dtype, s);
     rc = launch_amax(src, src_dtype, n, d_amax, s);
     if (rc) return rc;
     return launch_scaled_cast(src, src_dtype, dst, fp8_dtype, d_amax, d_scale_inv, n, compat, s);
@@ -516,13 +528,12 @@ cudaError_t cast_launch(const StreamArgs<kGroupMaxChunks>& args, int compat, cud
 }
 
 template <int SRC>
-int cast_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, const float* d_amax,
-                  float* d_scale_inv, int fp8_dtype, int compat, cudaStream_t s) {
+int cast_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, const float* d_amax, int fp8_dtype,
+                  int compat, cudaStream_t s) {
     StreamArgs<kGroupMaxChunks>& args = g_cast_args;
     for (int first = 0; first < static_cast<int>(idx.size()); first += kGroupMaxChunks) {
         const int count = std::min<int>(kGroupMaxChunks, static_cast<int>(idx.size()) - first);
         args.amax = d_amax;
-        args.scale_inv = d_scale_inv;
         args.status = sticky_status_ptr();
         const int64_t tiles = fill_cast(args, chunks, idx.data(), first, count);
         if (tiles == 0) continue;
@@ -543,14 +554,16 @@ int launch_amax_pass(const mf_chunk_desc* chunks, int32_t n_chunks, float* d_ama
     return rc;
 }
 
-int launch_cast_pass(const mf_chunk_desc* chunks, int32_t n_chunks, const float* d_amax, float* d_scale_inv,
-                     int fp8_dtype, int compat, cudaStream_t s) {
+int launch_cast_pass(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors, const float* d_amax,
+                     float* d_scale_inv, int fp8_dtype, int compat, cudaStream_t s) {
     std::lock_guard<std::mutex> lock(g_group_mutex);
+    int rc = launch_scale_inv(d_amax, d_scale_inv, n_tensors, fp8_dtype, s);
+    if (rc) return rc;
     std::vector<int32_t> by[3];
     group_by_dtype(chunks, n_chunks, by);
-    int rc = cast_launches<MF_DT_BF16>(chunks, by[0], d_amax, d_scale_inv, fp8_dtype, compat, s);
-    if (!rc) rc = cast_launches<MF_DT_F16>(chunks, by[1], d_amax, d_scale_inv, fp8_dtype, compat, s);
-    if (!rc) rc = cast_launches<MF_DT_F32>(chunks, by[2], d_amax, d_scale_inv, fp8_dtype, compat, s);
+    rc = cast_launches<MF_DT_BF16>(chunks, by[0], d_amax, fp8_dtype, compat, s);
+    if (!rc) rc = cast_launches<MF_DT_F16>(chunks, by[1], d_amax, fp8_dtype, compat, s);
+    if (!rc) rc = cast_launches<MF_DT_F32>(chunks, by[2], d_amax, fp8_dtype, compat, s);
     return rc;
 }
 }  // namespace
@@ -570,7 +583,8 @@ extern "C" int mf_ckpt_cast_pass(const mf_chunk_desc* chunks, int32_t n_chunks, 
     if (rc) return rc;
     rc = check_fp8_mode("mf_ckpt_cast_pass", fp8_dtype, compat);
     if (rc) return rc;
-    return launch_cast_pass(chunks, n_chunks, d_amax, d_scale_inv, fp8_dtype, compat, static_cast<cudaStream_t>(stream));
+    return launch_cast_pass(chunks, n_chunks, n_tensors, d_amax, d_scale_inv, fp8_dtype, compat,
+                            static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int mf_ckpt_quant_fp8(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors, float* d_amax,
@@ -588,7 +602,7 @@ extern "C" int mf_ckpt_quant_fp8(const mf_chunk_desc* chunks, int32_t n_chunks, 
         rc = comm_allreduce_max(comm, d_amax, n_tensors, s);
         if (rc) return rc;
     }
-    return launch_cast_pass(chunks, n_chunks, d_amax, d_scale_inv, fp8_dtype, compat, s);
+    return launch_cast_pass(chunks, n_chunks, n_tensors, d_amax, d_scale_inv, fp8_dtype, compat, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -671,8 +685,8 @@ int noalloc_amax_launches(const mf_chunk_desc* chunks, int32_t n_chunks, float* 
 
 // Pass 2 over the chunks of one source dtype.  Caller holds g_group_mutex.
 template <int SRC>
-int noalloc_cast_launches(const mf_chunk_desc* chunks, int32_t n_chunks, const float* d_amax, float* d_scale_inv,
-                          int fp8_dtype, int compat, cudaStream_t s) {
+int noalloc_cast_launches(const mf_chunk_desc* chunks, int32_t n_chunks, const float* d_amax, int fp8_dtype,
+                          int compat, cudaStream_t s) {
     StreamArgs<kGroupMaxChunks>& args = g_cast_args;
     int32_t i = 0;
     while (i < n_chunks) {
@@ -692,7 +706,6 @@ int noalloc_cast_launches(const mf_chunk_desc* chunks, int32_t n_chunks, const f
         }
         if (count == 0) continue;
         args.amax = d_amax;
-        args.scale_inv = d_scale_inv;
         args.status = sticky_status_ptr();
         args.n_chunks = count;
         args.total_tiles = tiles;
@@ -735,9 +748,11 @@ extern "C" int mf_ckpt_quant_fp8_noalloc(const mf_chunk_desc* chunks, int32_t n_
         rc = comm_allreduce_max(comm, amax, n_tensors, s);
         if (rc) return rc;
     }
+    rc = launch_scale_inv(amax, d_scale_inv, n_tensors, fp8_dtype, s);
+    if (rc) return rc;
     std::lock_guard<std::mutex> lock(g_group_mutex);
-    rc = noalloc_cast_launches<MF_DT_BF16>(chunks, n_chunks, amax, d_scale_inv, fp8_dtype, compat, s);
-    if (!rc) rc = noalloc_cast_launches<MF_DT_F16>(chunks, n_chunks, amax, d_scale_inv, fp8_dtype, compat, s);
-    if (!rc) rc = noalloc_cast_launches<MF_DT_F32>(chunks, n_chunks, amax, d_scale_inv, fp8_dtype, compat, s);
+    rc = noalloc_cast_launches<MF_DT_BF16>(chunks, n_chunks, amax, fp8_dtype, compat, s);
+    if (!rc) rc = noalloc_cast_launches<MF_DT_F16>(chunks, n_chunks, amax, fp8_dtype, compat, s);
+    if (!rc) rc = noalloc_cast_launches<MF_DT_F32>(chunks, n_chunks, amax, fp8_dtype, compat, s);
     return rc;
 }

@@ -423,3 +423,25 @@ def test_ckpt_rejects(backend):
     assert lib().mf_ckpt_quant_fp8(arr, 1, 2, 1, None, E4M3, 0, None, None) == -1  # tensor 5 of 2
     arr = checkpoint.make_chunks([(1, 1, 10, 0, DType.FLOAT8_E4M3)])
     assert lib().mf_ckpt_quant_fp8(arr, 1, 1, 1, None, E4M3, 0, None, None) == -3
+
+
+def test_ckpt_scale_inv_covers_tensors_without_local_elements(backend, ref):
+    """A rank that holds no row of a tensor still reports that tensor's scale_inv (from the
+    all-reduced amax): here tensor 1 has an empty chunk and tensor 3 no chunk at all."""
+    sizes = {0: 5000, 1: 0, 2: 2048}
+    raws = {t: synthetic.normal_bf16(600 + t, max(n, 1), 0.0, 0.5)[:n] for t, n in sizes.items()}
+    amax_all = np.array([ref.amax(raws[0], BF16), 3.5, ref.amax(raws[2], BF16), 0.0], np.float32)
+    srcs = {t: to_device(raws[t], pad=16) for t in sizes}
+    dsts = {t: empty(max(n, 1) + 16) for t, n in sizes.items()}
+    am = to_device(amax_all)
+    si = empty(16)
+    chunks = checkpoint.make_chunks([(srcs[t].ptr, dsts[t].ptr, n, t, DType.BFLOAT16) for t, n in sizes.items()])
+    call("mf_ckpt_cast_pass", chunks, len(sizes), 4, am.ptr, si.ptr, E4M3, 0, None)
+    got = fetch(si, 16, np.float32)
+    for t in range(4):
+        assert float(got[t]) == ref.fp8_scale_inv(float(amax_all[t]), E4M3), t
+    for t, n in sizes.items():
+        if n:
+            bits_equal(fetch(dsts[t], n), ref.scaled_cast(raws[t], BF16, E4M3, float(amax_all[t])))
+    for b in list(srcs.values()) + list(dsts.values()) + [am, si]:
+        b.free()

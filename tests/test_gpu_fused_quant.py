@@ -445,3 +445,47 @@ def test_ckpt_scale_inv_covers_tensors_without_local_elements(backend, ref):
             bits_equal(fetch(dsts[t], n), ref.scaled_cast(raws[t], BF16, E4M3, float(amax_all[t])))
     for b in list(srcs.values()) + list(dsts.values()) + [am, si]:
         b.free()
+
+
+def test_ckpt_quantise_from_several_host_threads(backend, ref):
+    """cgo may call from any OS thread: four threads quantise four checkpoints at once, each on
+    its own stream, through the grouped launches that share the library's argument blocks."""
+    import threading
+
+    from manifesto_b200 import Stream
+    specs = small_layout()
+    sizes = [s.numel for s in specs]
+    jobs = []
+    for j in range(4):
+        raws = [synthetic.normal_bf16(7000 + 50 * j + t, n, 0.0, 0.01 * (j + 1)) for t, n in enumerate(sizes)]
+        srcs = [to_device(r) for r in raws]
+        dsts = [empty(n) for n in sizes]
+        jobs.append({"raws": raws, "srcs": srcs, "dsts": dsts, "am": empty(4 * len(sizes)),
+                     "si": empty(4 * len(sizes)), "stream": Stream(), "err": None})
+
+    def work(job):
+        try:
+            chunks = checkpoint.make_chunks([(s.ptr, d.ptr, n, t, DType.BFLOAT16)
+                                             for t, (s, d, n) in enumerate(zip(job["srcs"], job["dsts"], sizes))])
+            for _ in range(5):
+                checkpoint.quantise(chunks, len(sizes), len(sizes), job["am"].ptr, job["si"].ptr, DType.FLOAT8_E4M3,
+                                    0, None, job["stream"])
+            job["stream"].sync()
+        except Exception as e:  # reported below
+            job["err"] = e
+
+    threads = [threading.Thread(target=work, args=(job,)) for job in jobs]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=120)
+    for job in jobs:
+        assert job["err"] is None, job["err"]
+        si = fetch(job["si"], 4 * len(sizes), np.float32)
+        for t, (raw, d) in enumerate(zip(job["raws"], job["dsts"])):
+            a = ref.amax(raw, BF16)
+            assert float(si[t]) == ref.fp8_scale_inv(a, E4M3)
+            bits_equal(fetch(d, sizes[t]), ref.scaled_cast(raw, BF16, E4M3, a))
+        for b in job["srcs"] + job["dsts"] + [job["am"], job["si"]]:
+            b.free()
+        job["stream"].close()

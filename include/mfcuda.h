@@ -217,6 +217,14 @@ int mf_axpy(void* y, const void* x, int64_t n, float alpha, int dtype,
 enum mf_scalar_op { MF_SCALAR_ADD = 0, MF_SCALAR_SUB = 1, MF_SCALAR_MUL = 2, MF_SCALAR_DIV = 3 };
 int mf_scalar_broadcast(const void* src, int src_dtype, void* dst, int dst_dtype,
                         int64_t n, float scalar, int op, mf_stream stream);
+/* math.linspace (runtime/executor_math.go:57-108) written straight into device
+ * memory as F32, BF16 or F16 (the store encode of writeLinspaceOutput):
+ * v[i] = start + float32(i) * ((stop - start) / float32(intervals)), intervals =
+ * count - 1 (count when endpoint is 0), v[0] = start and v[count-1] = stop when the
+ * endpoint is included. count <= 0 is MF_ERR_INVALID_ARGUMENT ("count must be
+ * positive"). */
+int mf_linspace(float start, float stop, int64_t count, int endpoint, void* dst, int dst_dtype,
+                mf_stream stream);
 
 /* ---------------------------------------------------------------------
  * K7: fused elementwise chains (optimizer.FusionAST, optimizer/fusion_ast.go:86-113).

@@ -81,6 +81,7 @@ SIGNATURES: dict[str, list] = {
     "mf_int4_dequant_grouped": [_vp, _vp, _int, _vp, _int, _i64, _i64, _i64, _vp],
     "mf_axpy": [_vp, _vp, _i64, _f32, _int, _int, _vp],
     "mf_scalar_broadcast": [_vp, _int, _vp, _int, _i64, _f32, _int, _vp],
+    "mf_linspace": [_f32, _f32, _i64, _int, _vp, _int, _vp],
     "mf_fused_compile": [ctypes.POINTER(FusedProgram), ctypes.POINTER(_vp)],
     "mf_fused_destroy": [_vp],
     "mf_fused_is_specialised": [_vp, ctypes.POINTER(_int)],

@@ -335,6 +335,19 @@ class CUDABackend:
             call("mf_stream_sync", None)
         return t
 
+    def linspace(self, start: float, stop: float, count: int, endpoint: bool = True,
+                 dtype: DType = DType.FLOAT32, stream=None) -> DeviceTensor:
+        """math.linspace generated on the device in its storage dtype (F32, BF16 or F16)."""
+        self._check()
+        out = self.empty([int(count)], dtype)
+        try:
+            call("mf_linspace", float(start), float(stop), int(count), 1 if endpoint else 0, out.dispatch_pointer(),
+                 int(dtype), stream_handle(stream))
+        except BaseException:
+            out.close()
+            raise
+        return out
+
     def upload_float32_as(self, shape: Sequence[int], dtype: DType, values, stream=None) -> DeviceTensor:
         """Upload(shape, dtype, Float32AsDTypeBytes(values, dtype)) with the encode on the device.
 

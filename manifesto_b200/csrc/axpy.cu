@@ -194,6 +194,31 @@ void dispatch_scalar_dst(int dst_dt, int op, const void* src, void* dst, int64_t
     }
 }
 
+// math.linspace (runtime/executor_math.go:57-108): v[i] = start + float32(i) * step,
+// every operation rounded to float32 and nothing contracted, the endpoints pinned when
+// they are included, encoded with the store encoder.  With a finite start and step no
+// NaN can arise, so plain operations are exact; otherwise the amd64 NaN rule applies.
+template <int DT, bool SPECIAL>
+__global__ void __launch_bounds__(256) linspace_kernel(float start, float stop, float step, int64_t count,
+                                                       int pin_ends, void* __restrict__ dst) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += stride) {
+        const float fi = __ll2float_rn(i);
+        float v = SPECIAL ? x86_add(start, x86_mul(fi, step)) : __fadd_rn(start, __fmul_rn(fi, step));
+        if (count == 1 || (pin_ends && i == 0)) v = start;
+        if (pin_ends && i == count - 1) v = stop;
+        store_code<DT>(dst, i, encode_f32<DT>(v, 0));
+    }
+}
+
+template <int DT>
+void launch_linspace(float start, float stop, float step, int64_t count, int pin_ends, void* dst, cudaStream_t s) {
+    const unsigned blocks = static_cast<unsigned>(stream_grid(count, 256, 8));
+    const bool special = !(fabsf(start) <= 3.402823466e38f) || !(fabsf(step) <= 3.402823466e38f);
+    if (special) linspace_kernel<DT, true><<<blocks, 256, 0, s>>>(start, stop, step, count, pin_ends, dst);
+    else linspace_kernel<DT, false><<<blocks, 256, 0, s>>>(start, stop, step, count, pin_ends, dst);
+}
+
 }  // namespace
 }  // namespace mf
 
@@ -248,5 +273,27 @@ extern "C" int mf_scalar_broadcast(const void* src, int src_dtype, void* dst, in
     default: dispatch_scalar_dst<MF_DT_U8>(dst_dtype, op, src, dst, n, scalar, s); break;
     }
     MF_LAUNCH_CHECK("mf_scalar_broadcast launch");
+    return MF_OK;
+}
+
+extern "C" int mf_linspace(float start, float stop, int64_t count, int endpoint, void* dst, int dst_dtype,
+                           mf_stream stream) {
+    MF_ENTER();
+    if (count <= 0) return fail(MF_ERR_INVALID_ARGUMENT, "math.linspace: count must be positive");
+    if (dst_dtype != MF_DT_F32 && dst_dtype != MF_DT_BF16 && dst_dtype != MF_DT_F16)
+        return fail(MF_ERR_DTYPE_UNSUPPORTED, "mf_linspace: output dtype %d unsupported (F32, BF16, F16)", dst_dtype);
+    if (!dst) return fail(MF_ERR_INVALID_ARGUMENT, "mf_linspace: NULL buffer");
+    // the step in float32 on the host, as the reference computes it (x86-64 SSE arithmetic:
+    // the same rounding and NaN rule as Go on amd64)
+    const int64_t intervals = (endpoint || count == 1) ? count - 1 : count;
+    const float step = count == 1 ? 0.0f : (stop - start) / static_cast<float>(intervals);
+    const int pin_ends = (count > 1 && intervals == count - 1) ? 1 : 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (dst_dtype) {
+    case MF_DT_BF16: launch_linspace<MF_DT_BF16>(start, stop, step, count, pin_ends, dst, s); break;
+    case MF_DT_F16: launch_linspace<MF_DT_F16>(start, stop, step, count, pin_ends, dst, s); break;
+    default: launch_linspace<MF_DT_F32>(start, stop, step, count, pin_ends, dst, s); break;
+    }
+    MF_LAUNCH_CHECK("mf_linspace launch");
     return MF_OK;
 }

@@ -197,3 +197,103 @@ def write_float32_vector_output(values: dict[str, Any], reference: str, payload:
         if _is_tensor(output):
             output.close()
         raise
+
+
+# ------------------------------------------------------------- math.linspace
+
+def _required_float32(config: dict[str, Any], key: str) -> float:
+    """requiredFloat32FromConfig (runtime/executor_math.go:445-480)."""
+    if key not in config:
+        raise StateError(f"{key} is required")
+    raw = config[key]
+    if isinstance(raw, bool) or not isinstance(raw, (int, float, str, np.floating, np.integer)):
+        raise StateError(f"{key} must be numeric, got {_go_type(raw)}")
+    try:
+        return float(np.float32(float(raw)))
+    except ValueError as e:
+        raise StateError(str(e)) from None
+
+
+def _required_int(config: dict[str, Any], key: str) -> int:
+    """requiredIntFromConfig / requiredIntFromAny (runtime/executor_math.go:387-443)."""
+    if key not in config:
+        raise StateError(f"{key} is required")
+    raw = config[key]
+    if isinstance(raw, bool) or not isinstance(raw, (int, float, str, np.integer)):
+        raise StateError(f"expected integer, got {_go_type(raw)}")
+    if isinstance(raw, str):
+        # strconv.Atoi: an optional sign and decimal digits, nothing else
+        body = raw[1:] if raw[:1] in "+-" else raw
+        if not body.isascii() or not body.isdigit():
+            raise StateError(f'strconv.Atoi: parsing "{raw}": invalid syntax')
+        return int(raw)
+    return int(raw)
+
+
+def _float_dtype_from_config(config: dict[str, Any], fallback: DType) -> DType:
+    """floatDTypeFromConfig (runtime/executor_math.go:361-385)."""
+    if "dtype" not in config:
+        return fallback
+    raw = config["dtype"]
+    if not isinstance(raw, str):
+        raise StateError("dtype must be a string")
+    try:
+        fmt = parse(raw)
+    except ValueError as e:
+        raise StateError(str(e)) from None
+    if fmt not in FLOAT_DTYPES:
+        raise StateError(f"dtype {fmt.wire_name()} is not floating point")
+    return fmt
+
+
+def run_linspace(config: dict[str, Any], outputs: dict[str, str], values: dict[str, Any],
+                 state: StateStore | None, state_memory) -> None:
+    """runLinspace (runtime/executor_math.go:57-134) with the vector made on the device.
+
+    A "state.*" output becomes a resident tensor generated straight into its storage
+    dtype (no float32 host vector, no upload); any other output is the float32 host
+    copy the reference keeps (generated on the device and read back when device
+    memory is given).  Checks and messages follow the reference."""
+    def wrap(fn, *args):
+        try:
+            return fn(*args)
+        except StateError as e:
+            raise StateError(f"math.linspace: {e}") from None
+    start = wrap(_required_float32, config, "start")
+    stop = wrap(_required_float32, config, "stop")
+    count = wrap(_required_int, config, "count")
+    if count <= 0:
+        raise StateError("math.linspace: count must be positive")
+    endpoint = config.get("endpoint")
+    endpoint = endpoint if isinstance(endpoint, bool) else True
+    fmt = wrap(_float_dtype_from_config, config, DType.FLOAT32)
+    if not outputs:
+        raise StateError("runtime vector output requires at least one target")
+    host = None
+    for reference in outputs.values():
+        if reference.startswith("state.") and state is not None and state_memory is not None:
+            if fmt not in (DType.FLOAT32, DType.BFLOAT16, DType.FLOAT16):
+                # Float32AsDTypeBytes hands Upload float32 bytes for any other format
+                from .errors import ShapeMismatch
+                raise ShapeMismatch(f"tensor: shape ({count},) x {fmt.name} needs {fmt.bytes_for(count)} bytes, "
+                                    f"got {4 * count}")
+            t = state_memory.linspace(start, stop, count, endpoint, fmt)
+            try:
+                state.set(reference[len("state."):], t)
+            except Exception:
+                t.close()
+                raise
+            continue
+        if reference.startswith("state.") and state is None:
+            raise StateError(f'state output "{reference}" requires a state store')
+        if host is None:
+            if state_memory is not None:
+                t = state_memory.linspace(start, stop, count, endpoint, DType.FLOAT32)
+                host = np.frombuffer(t.raw_bytes(), np.float32).copy()
+                t.close()
+            else:
+                raise StateError("math.linspace: a device backend is required")
+        if reference.startswith("state."):
+            state.set(reference[len("state."):], host.copy())
+        else:
+            values[reference] = host.copy()

@@ -440,6 +440,34 @@ int ref_scalar_broadcast(const void* src, int src_dtype, void* dst, int dst_dtyp
     return 0;
 }
 
+/* runLinspace, runtime/executor_math.go:57-108: step = (stop - start) / float32(intervals)
+ * with intervals = count - 1 (count when endpoint is false); output[i] = start +
+ * float32(i) * step, each operation rounded to float32 (amd64: no contraction, the SSE
+ * NaN rule); with the endpoint included output[0] = start and output[count-1] = stop;
+ * count == 1 gives start.  Elements [begin, begin + n) are encoded with the store
+ * encoder (Float32AsDTypeBytes, runtime/session.go:431-452). */
+int ref_linspace(float start, float stop, int64_t count, int endpoint, void* dst, int dst_dtype,
+                 int64_t begin, int64_t n) {
+    if (count <= 0) return ERR_INVALID;
+    const int64_t intervals = (endpoint || count == 1) ? count - 1 : count;
+    const float step = count == 1 ? 0.0f : x86_div(x86_sub(stop, start), (float)intervals);
+    for (int64_t i = begin; i < begin + n; i++) {
+        float v;
+        if (count == 1) {
+            v = start;
+        } else {
+            v = x86_add(start, x86_mul((float)i, step));
+            if (intervals == count - 1) {
+                if (i == 0) v = start;
+                if (i == count - 1) v = stop;
+            }
+        }
+        int rc = encode_one(dst_dtype, v, dst, i, 0);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
 /* ------------------------------------------------------ fused evaluator */
 
 /* optimizer.NodeType, optimizer/fusion_ast.go:32-65 */

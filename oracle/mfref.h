@@ -52,6 +52,8 @@ int ref_int4_dequant_grouped(const uint8_t* q, const void* scales, int scale_dty
 
 int ref_axpy(void* y, const void* x, int64_t begin, int64_t n, float alpha, int dtype, int fused_fma);
 
+int ref_linspace(float start, float stop, int64_t count, int endpoint, void* dst, int dst_dtype,
+                 int64_t begin, int64_t n);
 int ref_scalar_broadcast(const void* src, int src_dtype, void* dst, int dst_dtype,
                          int64_t begin, int64_t n, float scalar, int op);
 

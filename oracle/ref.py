@@ -55,6 +55,7 @@ def lib() -> ctypes.CDLL:
             ("ref_int4_dequant_grouped", ctypes.c_int, [vp, vp, ctypes.c_int, vp, ctypes.c_int, i64, i64, i64, i64, i64]),
             ("ref_axpy", ctypes.c_int, [vp, vp, i64, i64, ctypes.c_float, ctypes.c_int, ctypes.c_int]),
             ("ref_scalar_broadcast", ctypes.c_int, [vp, ctypes.c_int, vp, ctypes.c_int, i64, i64, ctypes.c_float, ctypes.c_int]),
+            ("ref_linspace", ctypes.c_int, [ctypes.c_float, ctypes.c_float, i64, ctypes.c_int, vp, ctypes.c_int, i64, i64]),
             ("ref_fused_eval", ctypes.c_int, [ctypes.c_int, vp, vp, vp, vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, vp,
                                               vp, ctypes.c_int, i64, i64]),
             ("ref_amax", u32, [vp, ctypes.c_int, i64, i64]),
@@ -148,6 +149,16 @@ def scalar_broadcast(src: np.ndarray, src_dtype: int, dst_dtype: int, scalar: fl
     _parallel(lambda b, c: L.ref_scalar_broadcast(_ptr(src), src_dtype, _ptr(out), dst_dtype, b, c, scalar, op), n,
               threads, align=2)
     return out.view({2: np.uint16, 4: np.uint32}[ITEMSIZE[dst_dtype]])
+
+
+def linspace(start: float, stop: float, count: int, endpoint: bool = True, dst_dtype: int = F32,
+             threads: int = 1) -> np.ndarray:
+    """runLinspace (runtime/executor_math.go:57-108) stored as dst_dtype; returns raw codes."""
+    out = np.empty(count * ITEMSIZE[dst_dtype], dtype=np.uint8)
+    L = lib()
+    _parallel(lambda b, c: L.ref_linspace(start, stop, count, 1 if endpoint else 0, _ptr(out), dst_dtype, b, c),
+              count, threads)
+    return out
 
 
 def fused_eval(tree: dict, inputs: list[np.ndarray], in_dtypes: list[int], in_bcast: list[int], out_dtype: int,

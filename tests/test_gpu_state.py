@@ -49,3 +49,29 @@ def test_store_path_and_reference_byte_count_failure(backend, ref):
     # Float32AsDTypeBytes passes FP8 through as float32 bytes, which Upload rejects
     with pytest.raises(ShapeMismatch):
         backend.upload_float32_as([64, 64], DType.FLOAT8_E4M3, v)
+
+
+@pytest.mark.parametrize("start,stop,count,endpoint", [
+    (0.0, 1.0, 1, True), (0.0, 1.0, 2, True), (0.0, 1.0, 5, False), (-3.25, 17.5, 100003, True),
+    (1e30, -1e30, 4097, False), (0.0, 1.0, (1 << 24) + 17, True), (float("nan"), 2.0, 33, True),
+    (1.0, float("inf"), 9, True), (5.0, 5.0, 1000, False)])
+@pytest.mark.parametrize("dt,oracle_dt", [(DType.FLOAT32, F32), (DType.BFLOAT16, BF16), (DType.FLOAT16, F16)])
+def test_linspace_bit_exact(backend, ref, start, stop, count, endpoint, dt, oracle_dt):
+    t = backend.linspace(start, stop, count, endpoint, dt)
+    assert t.shape() == (count,) and t.dtype() == dt
+    want = ref.linspace(start, stop, count, endpoint, oracle_dt, threads=4)
+    assert backend.download(t)[1] == want.tobytes()
+    t.close()
+
+
+def test_run_linspace_on_the_device(backend, ref):
+    st, values = state.StateStore(), {}
+    state.run_linspace({"start": -1, "stop": 1, "count": 257, "dtype": "f16"},
+                       {"grid": "state.grid", "copy": "grid_host"}, values, st, backend)
+    g = st.get("grid")[0]
+    assert g.dtype() == DType.FLOAT16 and backend.download(g)[1] == ref.linspace(-1.0, 1.0, 257, True, F16).tobytes()
+    assert values["grid_host"].tobytes() == ref.linspace(-1.0, 1.0, 257, True, F32).tobytes()
+    g.close()
+    with pytest.raises(ShapeMismatch):  # Float32AsDTypeBytes passes FP8 through as float32 bytes
+        state.run_linspace({"start": 0, "stop": 1, "count": 8, "dtype": "F8_E4M3"}, {"q": "state.q"}, values, st,
+                           backend)

@@ -224,3 +224,43 @@ def test_scaled_cast_rule(ref):
     # the element equal to amax scales to exactly 448 -> code 0x7e
     xf = ref.convert(x, ref.BF16, ref.F32).view(np.float32)
     assert q[np.argmax(np.abs(xf))] & 0x7F == 0x7E
+
+
+def _np_linspace(start, stop, count, endpoint=True):
+    """runLinspace restated with numpy float32 scalars (IEEE, no contraction)."""
+    f = np.float32
+    if count == 1:
+        return np.array([start], np.float32)
+    intervals = count - 1 if endpoint else count
+    step = (f(stop) - f(start)) / f(intervals)
+    idx = np.arange(count, dtype=np.int64).astype(np.float32)
+    out = (f(start) + idx * step).astype(np.float32)
+    if endpoint:
+        out[0], out[-1] = f(start), f(stop)
+    return out
+
+
+def test_linspace_known_answers(ref):
+    assert ref.linspace(0.0, 1.0, 5).view(np.float32).tolist() == [0.0, 0.25, 0.5, 0.75, 1.0]
+    got = ref.linspace(0.0, 1.0, 5, endpoint=False).view(np.float32)
+    assert got.tolist() == [np.float32(i) * np.float32(0.2) for i in range(5)]
+    assert ref.linspace(3.5, -7.0, 1).view(np.float32).tolist() == [3.5]
+    # the endpoint is stop exactly even where start + (n-1)*step rounds elsewhere
+    g = ref.linspace(0.1, 0.7, 7).view(np.float32)
+    assert g[-1] == np.float32(0.7) and g[0] == np.float32(0.1)
+
+
+@pytest.mark.parametrize("start,stop,count,endpoint", [
+    (0.0, 1.0, 1001, True), (-3.25, 17.5, 4097, False), (1e30, -1e30, 77, True),
+    (0.0, 1.0, (1 << 24) + 5, True), (5.0, 5.0, 10, True)])
+def test_linspace_matches_float32_restatement(ref, start, stop, count, endpoint):
+    got = ref.linspace(start, stop, count, endpoint, threads=4).view(np.float32)
+    assert np.array_equal(got, _np_linspace(start, stop, count, endpoint))
+
+
+def test_linspace_nan_and_encoders(ref):
+    v = ref.linspace(float("nan"), 1.0, 9).view(np.uint32)
+    assert (v[:-1] == 0x7FC00000).all() and v[-1] == np.float32(1.0).view(np.uint32)
+    for dt in (ref.BF16, ref.F16):
+        f32 = ref.linspace(-2.0, 3.0, 1000)
+        assert ref.linspace(-2.0, 3.0, 1000, dst_dtype=dt).tobytes() == ref.convert(f32, ref.F32, dt).tobytes()

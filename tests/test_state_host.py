@@ -93,3 +93,41 @@ def test_write_float32_vector_output():
     assert isinstance(st.get("k")[0], np.ndarray)
     with pytest.raises(state.StateError, match='state output "state.h" requires a state store'):
         state.write_float32_vector_output(values, "state.h", payload, None, mem)
+
+
+class FakeLinspaceMemory(FakeMemory):
+    def linspace(self, start, stop, count, endpoint=True, dtype=DType.FLOAT32, stream=None):
+        self.calls.append(("linspace", start, stop, count, endpoint, DType(dtype)))
+        t = FakeTensor((count,), dtype, "linspace")
+        t.raw_bytes = lambda: np.arange(count, dtype=np.float32).tobytes()
+        return t
+
+
+def test_run_linspace_routes_outputs_and_parses_config():
+    mem, st, values = FakeLinspaceMemory(), state.StateStore(), {}
+    cfg = {"start": "0.5", "stop": 2, "count": 4.0, "endpoint": False, "dtype": "bf16"}
+    state.run_linspace(cfg, {"a": "state.grid", "b": "plain"}, values, st, mem)
+    assert mem.calls[0] == ("linspace", 0.5, 2.0, 4, False, DType.BFLOAT16)
+    assert st.get("grid")[0].how == "linspace"
+    assert mem.calls[1][5] == DType.FLOAT32 and values["plain"].tolist() == [0.0, 1.0, 2.0, 3.0]
+    state.run_linspace({"start": 1, "stop": 3, "count": "3"}, {"x": "v"}, values, st, mem)  # defaults: endpoint, F32
+    assert mem.calls[-1][1:] == (1.0, 3.0, 3, True, DType.FLOAT32)
+
+
+@pytest.mark.parametrize("cfg,msg", [
+    ({"stop": 1, "count": 2}, "math.linspace: start is required"),
+    ({"start": [1], "stop": 1, "count": 2}, "math.linspace: start must be numeric, got list"),
+    ({"start": 0, "stop": 1}, "math.linspace: count is required"),
+    ({"start": 0, "stop": 1, "count": " 5"}, 'math.linspace: strconv.Atoi: parsing " 5": invalid syntax'),
+    ({"start": 0, "stop": 1, "count": 0}, "math.linspace: count must be positive"),
+    ({"start": 0, "stop": 1, "count": 3, "dtype": 5}, "math.linspace: dtype must be a string"),
+    ({"start": 0, "stop": 1, "count": 3, "dtype": "i32"}, "math.linspace: dtype I32 is not floating point"),
+])
+def test_run_linspace_errors(cfg, msg):
+    with pytest.raises(state.StateError, match="^" + msg.replace("(", r"\(").replace(")", r"\)") + "$"):
+        state.run_linspace(cfg, {"o": "v"}, {}, state.StateStore(), FakeLinspaceMemory())
+
+
+def test_run_linspace_needs_a_target():
+    with pytest.raises(state.StateError, match="requires at least one target"):
+        state.run_linspace({"start": 0, "stop": 1, "count": 3}, {}, {}, state.StateStore(), FakeLinspaceMemory())

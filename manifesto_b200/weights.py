@@ -288,6 +288,7 @@ def quantize_file(src: str | os.PathLike, dst: str | os.PathLike, fp8_dtype: DTy
     fin = os.open(src, os.O_RDONLY)
     fout = os.open(dst, os.O_RDWR | os.O_CREAT | os.O_TRUNC, 0o644)
     streams = slots = None
+    ok = False
     try:
         os.ftruncate(fout, obase + data_size)
         _pwrite_all(fout, memoryview(header), 0)
@@ -356,6 +357,7 @@ def quantize_file(src: str | os.PathLike, dst: str | os.PathLike, fp8_dtype: DTy
                     flush(s)
         rep.quantized = len(qlist)
         rep.dst_bytes = obase + data_size
+        ok = True
     finally:
         if slots:
             for s in slots:
@@ -370,5 +372,7 @@ def quantize_file(src: str | os.PathLike, dst: str | os.PathLike, fp8_dtype: DTy
                 st.close()
         os.close(fin)
         os.close(fout)
+        if not ok:
+            os.unlink(dst)  # no half-written checkpoint is left behind
     rep.seconds = time.perf_counter() - t_start
     return rep

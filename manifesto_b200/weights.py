@@ -16,7 +16,7 @@ F8_E5M2) tensor with the same shape plus a float32 scalar "<name>_scale_inv"
 (amax / fp8_max; 1 for an all-zero or non-finite tensor); everything else is
 copied through.  Tensors stream through the GPU in batches over two device
 slots: while batch i is on the device (upload, two kernel passes, download on
-three CUDA streams), the host writes batch i-1's codes and reads batch i+1 from
+three CUDA streams), host threads write batch i-1's codes and read batch i+1 from
 the file straight into page-locked memory.  The codes are the ones
 mf_ckpt_quant_fp8 produces, so they are bit-identical to the oracle's
 scaled cast of each tensor.
@@ -28,6 +28,7 @@ import json
 import os
 import struct
 import time
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 from typing import BinaryIO, Callable, Sequence
 
@@ -214,14 +215,23 @@ def _pwrite_all(fd: int, buf: memoryview, offset: int) -> None:
         done += os.pwrite(fd, buf[done:], offset + done)
 
 
+_IO_PIECE = 64 << 20  # bytes per pread/pwrite job (the calls release the GIL and run in parallel)
+
+
+def _pieces(buf: memoryview, offset: int) -> list[tuple[memoryview, int]]:
+    return [(buf[p: p + _IO_PIECE], offset + p) for p in range(0, len(buf), _IO_PIECE)] or [(buf, offset)]
+
+
 def quantize_file(src: str | os.PathLike, dst: str | os.PathLike, fp8_dtype: DType = DType.FLOAT8_E4M3,
                   compat: int = 0, select: Callable[[str, TensorMeta], bool] | None = None,
-                  batch_bytes: int = 1 << 30, suffix: str = "_scale_inv") -> QuantizeReport:
+                  batch_bytes: int = 1 << 30, suffix: str = "_scale_inv",
+                  io_threads: int = min(8, os.cpu_count() or 2)) -> QuantizeReport:
     """Quantise the SafeTensors checkpoint at src into a new file at dst (see the module text).
 
     batch_bytes bounds the source bytes per device slot (a larger tensor gets a
-    slot of its own size); the device holds two slots.  Needs an initialised
-    backend (CUDABackend) on the current device."""
+    slot of its own size); the device holds two slots.  File reads and writes run
+    on io_threads threads in 64 MB pieces.  Needs an initialised backend
+    (CUDABackend) on the current device."""
     from ._abi import call
     from .backend import DeviceBuffer, Event, PinnedBuffer, Stream
     from .checkpoint import make_chunks, quantise
@@ -289,6 +299,7 @@ def quantize_file(src: str | os.PathLike, dst: str | os.PathLike, fp8_dtype: DTy
     fout = os.open(dst, os.O_RDWR | os.O_CREAT | os.O_TRUNC, 0o644)
     streams = slots = None
     ok = False
+    pool = ThreadPoolExecutor(max_workers=max(2, min(io_threads, 32)))
     try:
         os.ftruncate(fout, obase + data_size)
         _pwrite_all(fout, memoryview(header), 0)
@@ -313,29 +324,36 @@ def quantize_file(src: str | os.PathLike, dst: str | os.PathLike, fp8_dtype: DTy
                               "da": DeviceBuffer(4 * slot_t), "dsi": DeviceBuffer(4 * slot_t),
                               "up": Event(), "comp": Event(), "down": Event(), "batch": None, "plan": None})
 
-            def flush(s) -> None:
-                s["down"].sync()
+            def write_jobs(s) -> list:
+                """The slot's finished batch as write jobs (its download must have completed)."""
                 hd = _view(s["hd"].ptr, slot_dst)
                 sinv = (ctypes.c_float * slot_t).from_address(s["hsi"].ptr)
+                jobs = []
                 for k, (i, so, do) in enumerate(s["plan"]):
                     name, m, _, e, es = qlist[i]
-                    _pwrite_all(fout, hd[do: do + m.numel], obase + e.offset)
-                    _pwrite_all(fout, memoryview(struct.pack("<f", sinv[k])), obase + es.offset)
+                    jobs += _pieces(hd[do: do + m.numel], obase + e.offset)
+                    jobs.append((memoryview(struct.pack("<f", sinv[k])), obase + es.offset))
                     rep.scale_inv[name] = float(sinv[k])
                 s["batch"] = None
+                return [pool.submit(_pwrite_all, fout, buf, off) for buf, off in jobs]
 
             for bi, bt in enumerate(batches):
                 s = slots[bi % len(slots)]
+                writes = []
                 if s["batch"] is not None:
-                    flush(s)
-                plan, so, do = [], 0, 0
+                    s["down"].sync()
+                    writes = write_jobs(s)  # the slot's previous codes go out while its next batch comes in
+                plan, so, do, reads = [], 0, 0, []
                 hs = _view(s["hs"].ptr, slot_src)
                 for i in bt:
                     _, m, _, _, _ = qlist[i]
-                    _pread_into(fin, hs[so: so + m.nbytes], base + m.data_offsets[0])
+                    reads += [pool.submit(_pread_into, fin, buf, off)
+                              for buf, off in _pieces(hs[so: so + m.nbytes], base + m.data_offsets[0])]
                     plan.append((i, so, do))
                     so += _up(m.nbytes)
                     do += _up(m.numel)
+                for f in reads:
+                    f.result()
                 entries = [(s["ds"].ptr + so_, s["dd"].ptr + do_, qlist[i][1].numel, k, qlist[i][2])
                            for k, (i, so_, do_) in enumerate(plan)]
                 call("mf_memcpy_h2d_async", s["ds"].ptr, s["hs"].ptr, so, up.handle)
@@ -344,6 +362,8 @@ def quantize_file(src: str | os.PathLike, dst: str | os.PathLike, fp8_dtype: DTy
                 quantise(make_chunks(entries), len(entries), len(entries), s["da"].ptr, s["dsi"].ptr, fp8_dtype,
                          compat, None, comp)
                 s["comp"].record(comp)
+                for f in writes:  # the slot's download buffers are reused next
+                    f.result()
                 down.wait(s["comp"])
                 call("mf_memcpy_d2h_async", s["hd"].ptr, s["dd"].ptr, do, down.handle)
                 call("mf_memcpy_d2h_async", s["hsi"].ptr, s["dsi"].ptr, 4 * len(entries), down.handle)
@@ -354,7 +374,9 @@ def quantize_file(src: str | os.PathLike, dst: str | os.PathLike, fp8_dtype: DTy
                 rep.src_bytes += sum(qlist[i][1].nbytes for i in bt)
             for s in slots:
                 if s["batch"] is not None:
-                    flush(s)
+                    s["down"].sync()
+                    for f in write_jobs(s):
+                        f.result()
         rep.quantized = len(qlist)
         rep.dst_bytes = obase + data_size
         ok = True
@@ -370,6 +392,7 @@ def quantize_file(src: str | os.PathLike, dst: str | os.PathLike, fp8_dtype: DTy
         if streams:
             for st in streams:
                 st.close()
+        pool.shutdown(wait=True)
         os.close(fin)
         os.close(fout)
         if not ok:

@@ -17,7 +17,8 @@ through the C ABI (mf_ckpt_quant_fp8).
   kernels    (N=1) every other benchmark config as its own kernel line: FP8->FP32
              decode, Int4 group dequant, axpy f32/bf16, fused SwiGLU->FP8
   cpu_baseline  (N=1, rank 0) the C oracle port of the Go loops on the host cores,
-             on a bounded sample (decoder layer 0: 218,112,000 params)
+             on a bounded sample (decoder layer 0: 218,112,000 params); each kernel
+             line carries its own config's port timing under "cpu"
 
 --impl reference times that CPU port alone (the reference is Go; no Go toolchain
 exists on these machines, so the port stands in for it).
@@ -203,7 +204,7 @@ def kernel_line(name: str, alg_bytes: float, times_ms: list[float], peak: float,
 KERNEL_CONFIGS = ("c1", "c2", "c3", "c4")
 
 
-def bench_kernels(torch, stream_handle: int, peak: float, which=KERNEL_CONFIGS, reps: int = 20) -> dict:
+def bench_kernels(torch, stream_handle: int, peak: float, which=KERNEL_CONFIGS, reps: int = 50) -> dict:
     """Configs 1-4 on one GPU, each kernel timed alone with L2 flushed before every launch."""
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
     flush_words = flush_buf.view(torch.int64)
@@ -298,14 +299,14 @@ def _kernel_c4(torch, stream_handle, peak, flush, reps) -> dict:
     f = lambda: k.run_fp8(ptrs, pre.data_ptr(), qo.data_ptr(), n, am.data_ptr(), si.data_ptr(), stream=stream_handle)
     _warm(f)
     out["c4_fused_swiglu_fp8"] = kernel_line("swiglu_rows_kernel + stream_kernel<CastOp<BF16,E4M3>>", 9 * n,
-                                             time_launches(torch, f, max(5, reps // 2), flush), peak, n)
+                                             time_launches(torch, f, reps, flush), peak, n)
     f1 = lambda: k.run(ptrs, pre.data_ptr(), n, amax=am.data_ptr(), stream=stream_handle)
     out["c4_pass1_swiglu"] = kernel_line("swiglu_rows_kernel<amax>", 6 * n,
-                                         time_launches(torch, f1, max(5, reps // 2), flush), peak, n)
+                                         time_launches(torch, f1, reps, flush), peak, n)
     f2 = lambda: call("mf_fp8_scaled_cast", pre.data_ptr(), 4, qo.data_ptr(), 5, am.data_ptr(), si.data_ptr(), n, 0,
                       stream_handle)
     out["c4_pass2_cast"] = kernel_line("stream_kernel<CastOp<BF16,E4M3>>", 3 * n,
-                                       time_launches(torch, f2, max(5, reps // 2), flush), peak, n)
+                                       time_launches(torch, f2, reps, flush), peak, n)
     out["c4_fused_swiglu_fp8"]["single_pass_lower_bound_bytes"] = 5 * n
     k.close()
     return out
@@ -411,6 +412,9 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
         kernels = bench_kernels(torch, stream, peak, tuple(args.kernels.split(",")))
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(steps=2, warmup=0)
+        if kernels:
+            for key, c in cpu_kernel_baselines(tuple(args.kernels.split(","))).items():
+                kernels[key]["cpu"] = c
 
     if comm is not None:
         comm.close()
@@ -524,6 +528,63 @@ def cpu_baseline(steps: int, warmup: int, tensors=None) -> dict:
             "s_per_step": dt, "cpu": cpu_model(),
             "single_thread": {"value": one.size / dt1, "unit": "elems/s", "cores": 1,
                               "sample": f"the first tensor of the sample ({one.size:,} params), one pass"}}
+
+
+def _cpu_time(fn, threads: int) -> float:
+    fn(threads)  # warm: page in the output, build the thread pool
+    t = time.perf_counter()
+    fn(threads)
+    return time.perf_counter() - t
+
+
+def cpu_kernel_baselines(which=KERNEL_CONFIGS) -> dict:
+    """The oracle's C restatement of each config's Go loop on a bounded sample of that config, with the
+    config's value distribution: on every host thread and on one (the Go loops are single-goroutine)."""
+    import numpy as np
+
+    from manifesto_b200 import fusion, synthetic
+    from oracle import ref
+    cores = os.cpu_count() or 1
+    out = {}
+
+    def leg(key, n, fn, sample):
+        t_all, t_one = _cpu_time(fn, cores), _cpu_time(fn, 1)
+        out[key] = {"elems_per_s": n / t_all, "cores": cores, "single_thread_elems_per_s": n / t_one,
+                    "kind": "port", "sample": sample}
+
+    if "c1" in which:
+        n = 1 << 24
+        b = synthetic.uniform_bytes(0x5EED0001, n)
+        leg("c1_fp8e4m3_to_f32", n, lambda th: ref.convert(b, ref.E4M3, ref.F32, threads=th),
+            "convert.BytesToFloat32 (E4M3) over 2^24 uniform bytes (a quarter of config 1)")
+    if "c2" in which:
+        rows, cols, group = 512, 14336, 128
+        q = synthetic.uniform_bytes(0x5EED0002, rows * cols // 2)
+        sc = synthetic.abs_normal_bf16(0x5EED1002, rows * cols // group, 0.02)
+        leg("c2_int4_to_bf16", rows * cols,
+            lambda th: ref.int4_dequant(q, sc, ref.BF16, ref.BF16, rows, cols, group, threads=th),
+            "Int4 group dequant of 512 of the 4096 rows of config 2 (14336 cols, group 128)")
+    if "c3" in which:
+        n = 1 << 24
+        x, y = synthetic.normal_f32(0x5EED0003, n), synthetic.normal_f32(0x5EED1003, n)
+        leg("c3a_axpy_f32", n, lambda th: ref.axpy(y.copy(), x, 0.75, ref.F32, threads=th),
+            "axpyOntoHost f32 over 2^24 elements (1/16 of config 3), copy of y included")
+        xb, yb = synthetic.f32_to_bf16_bits(x), synthetic.f32_to_bf16_bits(y)
+        leg("c3b_axpy_bf16", n, lambda th: ref.axpy(yb.copy(), xb, 0.75, ref.BF16, threads=th),
+            "axpyOntoHost bf16 over 2^24 elements (1/16 of config 3), copy of y included")
+    if "c4" in which:
+        hidden, n = 4096, 1 << 22
+        ins = [synthetic.normal_bf16(0x5EED0004, n), synthetic.normal_bf16(0x5EED1004, hidden, 1.0, 0.1),
+               synthetic.normal_bf16(0x5EED2004, hidden, 0.0, 0.1), synthetic.normal_bf16(0x5EED3004, n)]
+        tree = fusion.node_table(fusion.swiglu_chain().root)
+
+        def c4(th):
+            pre = ref.fused_eval(tree, ins, [ref.BF16] * 4, [0, hidden, hidden, 0], ref.BF16, n, threads=th)
+            ref.scaled_cast(pre, ref.BF16, ref.E4M3, ref.amax(pre, ref.BF16, threads=th), threads=th)
+        leg("c4_fused_swiglu_fp8", n, c4,
+            "evalCPU of Mul(Silu(Add(Mul(x,g),b)),y) to BF16, amax, scaled E4M3 cast over 2^22 elements "
+            "(1/128 of config 4)")
+    return out
 
 
 def cpu_model() -> str:

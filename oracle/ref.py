@@ -89,9 +89,11 @@ def _ranges(n: int, threads: int, align: int = 1):
     return out
 
 
-def _parallel(fn, n: int, threads: int, align: int = 1):
+def _parallel(fn, n: int, threads: int, align: int = 1, work: int | None = None):
+    """Split [0, n) over threads; `work` (default n) is the element count the small-job cutoff compares,
+    for callers that split rows rather than elements."""
     rcs = []
-    if threads <= 1 or n < 1 << 16:
+    if threads <= 1 or (n if work is None else work) < 1 << 16:
         rcs.append(fn(0, n))
     else:
         with ThreadPoolExecutor(threads) as ex:
@@ -125,7 +127,8 @@ def int4_dequant(q: np.ndarray, scales: np.ndarray, scale_dtype: int, out_dtype:
     out = np.empty(rows * cols * ITEMSIZE[out_dtype], dtype=np.uint8)
     L = lib()
     _parallel(lambda b, c: L.ref_int4_dequant_grouped(_ptr(q), _ptr(scales), scale_dtype, _ptr(out), out_dtype,
-                                                      rows, cols, group, b, b + c), rows, threads)
+                                                      rows, cols, group, b, b + c), rows, threads,
+              work=rows * cols)
     return out.view({2: np.uint16, 4: np.uint32}[ITEMSIZE[out_dtype]])
 
 

@@ -139,6 +139,18 @@ class DeviceBuffer:
         self.free()
 
 
+class DeviceView(DeviceBuffer):
+    """`nbytes` at `ptr` inside an allocation someone else owns (a slot of a graph's
+    workspace): a tensor over it never frees it."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.ptr = int(ptr)
+        self.nbytes = int(nbytes)
+
+    def free(self) -> None:
+        self.ptr = 0
+
+
 class PinnedBuffer:
     """Page-locked host memory viewed as a numpy byte array."""
 

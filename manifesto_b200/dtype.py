@@ -44,6 +44,8 @@ class DType(enum.IntEnum):
             return (elements + 1) // 2
         if self == DType.BOOL:
             return (elements + 7) // 8
+        if self.size == 0:
+            raise ValueError(f"dtype: unsupported dtype {int(self)}")
         return elements * self.size
 
     def logical_elements(self, nbytes: int) -> int:

@@ -28,15 +28,25 @@ flat tables before the first dispatch; a node waits (cudaStreamWaitEvent) on its
 barriers, runs on its stream, then records (cudaEventRecord) its signal barriers.
 schedule_streams restates the scheduler over this module's Graph (edges are input
 names produced by earlier nodes) so a schedule can be made without the Go compiler.
+
+Workspace: GraphBackend.attach_workspace is runtime.WorkspaceAttacher.AttachWorkspace
+(runtime/executor.go:28-48, called once per graph by runtime/orchestrator.go:193-217).
+It takes the planner's ir.Topology (workspace.plan_graph restates the planner, from the
+nodes' input_types / output_type and the graph's bindings), makes one device allocation
+of WorkspaceLayout.Size bytes and resolves every port to base + offset.  A call of that
+graph then copies its inputs into their slots and has every node write its own slot: no
+allocation per node or per call.
 """
 from __future__ import annotations
 
 from dataclasses import dataclass, field
 from typing import Any, Sequence
 
-from .backend import CUDABackend, DeviceTensor
-from .dtype import DType, parse
-from .errors import DTypeMismatch, InvalidArgument
+from . import workspace as wsp
+from ._abi import call
+from .backend import CUDABackend, DeviceBuffer, DeviceTensor, DeviceView, convert_raw, stream_handle
+from .dtype import DECODE_SOURCES, DType, parse
+from .errors import DTypeMismatch, DTypeUnsupported, InvalidArgument, ShapeMismatch
 from .fusion import CUDAKernel, Target
 
 SHAPE_CAST = "shape.cast"
@@ -53,6 +63,8 @@ class GraphNode:
     inputs: list[str] = field(default_factory=list)
     attributes: dict[str, Any] = field(default_factory=dict)
     metadata: dict[str, Any] = field(default_factory=dict)
+    input_types: list[wsp.PortType] = field(default_factory=list)   # set by the typer; read by the planner
+    output_type: wsp.PortType | None = None
 
 
 @dataclass
@@ -62,6 +74,7 @@ class Graph:
     inputs: list[str] = field(default_factory=list)
     outputs: dict[str, str] = field(default_factory=dict)
     execution_dtype: DType = DType.FLOAT32
+    bindings: dict[str, int] = field(default_factory=dict)   # the typer's SymbolMap
 
 
 @dataclass
@@ -179,19 +192,184 @@ def _dtype_attr(node: GraphNode, key: str) -> DType | None:
     return parse(raw) if isinstance(raw, str) else DType(int(raw))
 
 
+# ---------------------------------------------------------------- workspace
+
+@dataclass
+class _Slot:
+    """A port's place in an attached workspace."""
+    ptr: int
+    dtype: DType
+    dims: tuple
+    capacity: int       # bytes the plan reserved: the port's size at the plan's bindings
+
+    def resolve(self, bindings: dict[str, int], what: str) -> tuple[tuple[int, ...], int]:
+        try:
+            shape = tuple(wsp.resolve_dims(self.dims, bindings))
+        except wsp.PlanError as e:
+            raise InvalidArgument(f"{what}: {e}") from None
+        count = 1
+        for d in shape:
+            count *= d
+        nbytes = self.dtype.bytes_for(count)
+        if nbytes > self.capacity:
+            raise ShapeMismatch(f"{what}: {list(shape)} x {self.dtype.wire_name()} needs {nbytes} bytes; the "
+                                f"workspace plan reserved {self.capacity}")
+        return shape, nbytes
+
+
+def _signature(g: Graph) -> list[tuple]:
+    return [(n.id, n.op, tuple(n.inputs)) for n in g.nodes]
+
+
+def plan_hazards(graph: Graph, topology: wsp.Topology) -> tuple[list[tuple[int, ...]], set[int]]:
+    """What running `graph` inside `topology`'s workspace must order or save, from the plan:
+
+    * reuse_deps[k]: the earlier nodes (indices) that read or wrote a port whose bytes
+      node k's output overwrites (a port dead before node k runs; the allocator never
+      lets ports that are live together overlap).  On one stream execution order covers
+      them; across streams node k must wait for them.
+    * snapshot: the nodes whose output is a graph output that a later port's bytes
+      overwrite -- the planner's liveness ends a port at its last consumer and does not
+      count graph outputs as consumers (ir/planner.go:186-283), so such an output must be
+      copied out right after its producer runs."""
+    ivs = {iv.port_id: iv for iv in topology.workspace.allocations}
+    touched: dict[int, set[int]] = {}
+    for k, tn in enumerate(topology.nodes):
+        for p in list(tn.inputs) + list(tn.outputs):
+            if p is not None and p.id in ivs:
+                touched.setdefault(p.id, set()).add(k)
+
+    def overlapping(pid: int):
+        lo, hi = ivs[pid].offset, ivs[pid].offset + ivs[pid].size
+        for q, iv in ivs.items():
+            if q != pid and iv.offset < hi and lo < iv.offset + iv.size:
+                yield iv
+
+    reuse_deps: list[tuple[int, ...]] = []
+    for k, tn in enumerate(topology.nodes):
+        p = tn.outputs[0] if tn.outputs else None
+        deps: set[int] = set()
+        if p is not None and p.id in ivs:
+            for iv in overlapping(p.id):
+                if iv.end < ivs[p.id].start:
+                    deps |= {j for j in touched.get(iv.port_id, ()) if j < k}
+        reuse_deps.append(tuple(sorted(deps)))
+    index = {n.id: k for k, n in enumerate(graph.nodes)}
+    snapshot: set[int] = set()
+    for producer in graph.outputs.values():
+        k = index.get(producer)
+        if k is None or not topology.nodes[k].outputs:
+            continue
+        pid = topology.nodes[k].outputs[0].id
+        if pid in ivs and any(iv.start > ivs[pid].end for iv in overlapping(pid)):
+            snapshot.add(k)
+    return reuse_deps, snapshot
+
+
+class AttachedWorkspace:
+    """One graph's device arena with every port resolved to base + offset, made once by
+    GraphBackend.attach_workspace (runtime.WorkspaceAttacher.AttachWorkspace,
+    runtime/executor.go:28-48).
+
+    Two properties of the plan are handled here rather than trusted:
+    * the planner's liveness ends a port at its last consumer and knows nothing of graph
+      outputs, so a later node can be given a graph output's bytes: such an output
+      (`snapshot`) is copied out right after its producer runs; the others are returned
+      as views into the arena, valid until the next call of the graph;
+    * offset reuse follows execution order, not streams: under a multi-stream schedule a
+      node whose output overwrites a dead port's bytes first waits for every node that
+      read or wrote that port on another stream (`reuse_deps`)."""
+
+    def __init__(self, graph: Graph, topology: wsp.Topology):
+        if [t.name for t in topology.nodes] != [n.id for n in graph.nodes]:
+            raise InvalidArgument("workspace: the topology's nodes are not the graph's nodes in order")
+        layout = topology.workspace
+        self.signature = _signature(graph)
+        self.size = layout.size
+        self.bindings = dict(layout.bindings)
+        ivs = {iv.port_id: iv for iv in layout.allocations}
+        nodes: list[tuple[int, DType, tuple, int]] = []      # (offset, dtype, dims, capacity)
+        for tn in topology.nodes:
+            p = tn.outputs[0] if tn.outputs else None
+            if p is None or p.allocation is None or p.id not in ivs:
+                raise InvalidArgument(f"workspace: node {tn.name!r} has no output allocation")
+            nodes.append((p.allocation.base_offset, p.type.dtype, p.type.dims, wsp.port_byte_size(p, self.bindings)))
+        inputs: dict[str, tuple[int, DType, tuple, int]] = {}
+        for name in graph.inputs:
+            if not name:
+                continue
+            off = topology.input_ports.get(name)
+            port = next((tn.inputs[i] for gn, tn in zip(graph.nodes, topology.nodes)
+                         for i, ref in enumerate(gn.inputs) if ref == name), None)
+            if off is None or port is None:
+                raise InvalidArgument(f"workspace: graph input {name!r} has no workspace offset")
+            inputs[name] = (off, port.type.dtype, port.type.dims, wsp.port_byte_size(port, self.bindings))
+        self.reuse_deps, self.snapshot = plan_hazards(graph, topology)
+        align = max(layout.align, 1)
+        pad = align - 256 if align > 256 else 0          # mf_alloc returns 256-byte aligned memory
+        self.buffer = DeviceBuffer(max(layout.size, 1) + pad)
+        self.base = wsp.align_up(self.buffer.ptr, align) if align > 1 else self.buffer.ptr
+        self.node_slots = [_Slot(self.base + off, dt, dims, cap) for off, dt, dims, cap in nodes]
+        self.input_slots = {name: _Slot(self.base + off, dt, dims, cap) for name, (off, dt, dims, cap) in inputs.items()}
+
+    def contains(self, ptr: int) -> bool:
+        return self.base <= ptr < self.base + max(self.size, 1)
+
+    def close(self) -> None:
+        self.buffer.free()
+
+
 class GraphBackend:
-    """runtime.Backend for the device path: CallGraph over shape.cast and FuseOp nodes."""
+    """runtime.Backend for the device path: CallGraph over shape.cast and FuseOp nodes, and
+    runtime.WorkspaceAttacher: a graph with an attached workspace runs inside it."""
 
     def __init__(self, backend: CUDABackend, compat: int = 0):
         self.backend = backend
         self.compat = compat
+        self._workspaces: dict[str, AttachedWorkspace] = {}
 
+    # -- workspace ------------------------------------------------------------
+    def attach_workspace(self, graph_name: str, graph: Graph, topology: wsp.Topology | None = None) -> wsp.Topology:
+        """AttachWorkspace(graphName, graph, topology): allocate topology.workspace.size bytes
+        once and resolve every port to base + offset.  With no topology the plan is made
+        here (workspace.plan_graph, the graph's bindings).  Replaces an earlier attachment
+        of the same name."""
+        if topology is None:
+            topology = wsp.plan_graph(graph)
+        ws = AttachedWorkspace(graph, topology)
+        self.detach_workspace(graph_name)
+        self._workspaces[graph_name] = ws
+        return topology
+
+    def workspace(self, graph_name: str) -> AttachedWorkspace | None:
+        return self._workspaces.get(graph_name)
+
+    def detach_workspace(self, graph_name: str) -> None:
+        ws = self._workspaces.pop(graph_name, None)
+        if ws is not None:
+            call("mf_device_sync")      # a call may still run on a stream of the caller's
+            ws.close()
+
+    def close(self) -> None:
+        for name in list(self._workspaces):
+            self.detach_workspace(name)
+
+    # -- graph.call -----------------------------------------------------------
     def call_graph(self, request: GraphCallRequest, stream=None,
                    schedule: dict[str, NodeSchedule] | None = None) -> GraphCallResult:
         """Run the graph on `stream`, or on the streams of `schedule` (see the module text).
-        With a schedule the call returns after every stream has finished."""
+        With a schedule the call returns after every stream has finished.  A graph with an
+        attached workspace runs inside it: inputs are copied to their slots, every node
+        writes its slot, launch_bindings override the plan's bindings (each size at most
+        the planned one)."""
+        ws = self._workspaces.get(request.graph_name)
+        if ws is not None and ws.signature != _signature(request.graph):
+            raise InvalidArgument(f"graph.call {request.graph_name!r}: the attached workspace was planned for "
+                                  f"another graph")
+        bindings = {**ws.bindings, **request.launch_bindings} if ws is not None else {}
+        staged = self._stage_inputs(request, ws, bindings, stream)
         if schedule is None:
-            return self._call(request, lambda node: stream, None)
+            return self._call(request, staged, lambda k, node: stream, None, ws=ws, bindings=bindings)
         from .backend import Event, Stream
         nodes = request.graph.nodes
         for n in nodes:
@@ -202,64 +380,107 @@ class GraphBackend:
                             {b.stream_id for n in nodes for b in schedule[n.id].barriers})
         streams = {sid: Stream() for sid in stream_ids}
         events = {b.event_id: Event() for n in nodes for b in schedule[n.id].barriers}
+        sid_of = [schedule[n.id].stream_id for n in nodes]
+        reuse_wait = [[j for j in ws.reuse_deps[k] if sid_of[j] != sid_of[k]] if ws is not None else []
+                      for k in range(len(nodes))]
+        reuse_events = {j: Event() for deps in reuse_wait for j in deps}
         start = Event()
         try:
             # work already queued for the inputs on the caller's stream (the legacy
-            # default stream when none is given) comes first
+            # default stream when none is given), the input copies included, comes first
             start.record(stream)
             for st in streams.values():
                 st.wait(start)
 
-            def on_stream(node: GraphNode):
+            def on_stream(k: int, node: GraphNode):
                 sched = schedule[node.id]
                 for b in sched.barriers:
                     if b.wait:
                         streams[sched.stream_id].wait(events[b.event_id])
+                for j in reuse_wait[k]:
+                    streams[sched.stream_id].wait(reuse_events[j])
                 return streams[sched.stream_id]
 
-            def after(node: GraphNode) -> None:
+            def after(k: int, node: GraphNode) -> None:
                 for b in schedule[node.id].barriers:
                     if not b.wait:
                         events[b.event_id].record(streams[b.stream_id])
+                if k in reuse_events:
+                    reuse_events[k].record(streams[sid_of[k]])
 
-            return self._call(request, on_stream, after, sync=list(streams.values()))
+            return self._call(request, staged, on_stream, after, sync=list(streams.values()), ws=ws,
+                              bindings=bindings)
         finally:
             for st in streams.values():
                 st.sync()
-            for ev in events.values():
+            for ev in list(events.values()) + list(reuse_events.values()):
                 ev.close()
             for st in streams.values():
                 st.close()
             start.close()
 
-    def _call(self, request: GraphCallRequest, stream_for, after, sync=()) -> GraphCallResult:
+    def _stage_inputs(self, request: GraphCallRequest, ws: AttachedWorkspace | None, bindings: dict[str, int],
+                      stream) -> dict[str, DeviceTensor]:
         g = request.graph
         values: dict[str, DeviceTensor] = {}
         for name in g.inputs:
             if name not in request.inputs:
                 raise InvalidArgument(f"graph.call {request.graph_name!r}: missing input {name!r}")
-            values[name] = request.inputs[name]
-        produced: list[DeviceTensor] = []
+            t = request.inputs[name]
+            if ws is None or name not in ws.input_slots:
+                values[name] = t
+                continue
+            slot = ws.input_slots[name]
+            shape, nbytes = slot.resolve(bindings, f"graph.call {request.graph_name!r} input {name!r}")
+            if t.dtype() != slot.dtype:
+                raise DTypeMismatch(f"graph.call {request.graph_name!r}: input {name!r} is "
+                                    f"{t.dtype().wire_name()}, the plan says {slot.dtype.wire_name()}")
+            if t.nbytes() != nbytes:
+                raise ShapeMismatch(f"graph.call {request.graph_name!r}: input {name!r} holds {t.nbytes()} bytes, "
+                                    f"the plan's {list(shape)} x {slot.dtype.wire_name()} is {nbytes}")
+            if t.dispatch_pointer() != slot.ptr and nbytes:
+                call("mf_memcpy_d2d_async", slot.ptr, t.dispatch_pointer(), nbytes, stream_handle(stream))
+            values[name] = DeviceTensor(self.backend, shape, slot.dtype, DeviceView(slot.ptr, nbytes))
+        return values
+
+    def _call(self, request: GraphCallRequest, values: dict[str, DeviceTensor], stream_for, after, sync=(),
+              ws: AttachedWorkspace | None = None, bindings: dict[str, int] | None = None) -> GraphCallResult:
+        g = request.graph
+        produced: list[DeviceTensor] = []       # tensors this call allocated
+        snapshots: dict[str, DeviceTensor] = {}
         try:
-            for node in g.nodes:
+            for k, node in enumerate(g.nodes):
                 args = []
                 for ref in node.inputs:
                     if ref not in values:
                         raise InvalidArgument(f"graph.call {request.graph_name!r}: node {node.id!r} reads "
                                               f"unknown value {ref!r}")
                     args.append(values[ref])
-                out = self._run_node(node, args, stream_for(node))
+                st = stream_for(k, node)
+                out = None
+                if ws is not None:
+                    slot = ws.node_slots[k]
+                    shape, nbytes = slot.resolve(bindings, f"graph.call {request.graph_name!r} node {node.id!r}")
+                    out = DeviceTensor(self.backend, shape, slot.dtype, DeviceView(slot.ptr, nbytes))
+                res = self._run_node(node, args, st, out)
+                if ws is not None and k in ws.snapshot:
+                    copy = self.backend.empty(res.shape(), res.dtype())
+                    produced.append(copy)
+                    if res.nbytes():
+                        call("mf_memcpy_d2d_async", copy.dispatch_pointer(), res.dispatch_pointer(), res.nbytes(),
+                             stream_handle(st))
+                    snapshots[node.id] = copy
                 if after is not None:
-                    after(node)
-                if out is not None and all(out is not a for a in args):
-                    produced.append(out)
-                values[node.id] = out
+                    after(k, node)
+                if ws is None and res is not None and all(res is not a for a in args):
+                    produced.append(res)
+                values[node.id] = res
             outputs = {}
             for name, ref in g.outputs.items():
                 if ref not in values:
                     raise InvalidArgument(f"graph.call {request.graph_name!r}: output {name!r} refers to "
                                           f"unknown node {ref!r}")
-                outputs[name] = values[ref]
+                outputs[name] = snapshots.get(ref, values[ref])
         except BaseException:
             for st in sync:
                 st.sync()
@@ -275,14 +496,23 @@ class GraphBackend:
         return GraphCallResult(outputs)
 
     # -- nodes ----------------------------------------------------------------
-    def _run_node(self, node: GraphNode, args: list[DeviceTensor], stream) -> DeviceTensor:
+    def _run_node(self, node: GraphNode, args: list[DeviceTensor], stream, out: DeviceTensor | None) -> DeviceTensor:
         if node.op == SHAPE_CAST:
-            return self._cast(node, args, stream)
+            return self._cast(node, args, stream, out)
         if node.op == FUSE_OP:
-            return self._fusion(node, args, stream)
+            return self._fusion(node, args, stream, out)
         raise InvalidArgument(f"graph.call: op {node.op!r} (node {node.id!r}) is not supported by the CUDA backend")
 
-    def _cast(self, node: GraphNode, args: list[DeviceTensor], stream) -> DeviceTensor:
+    @staticmethod
+    def _check_out(node: GraphNode, out: DeviceTensor, dtype: DType, n: int) -> None:
+        if out.dtype() != dtype:
+            raise DTypeMismatch(f"graph.call: node {node.id!r} produces {dtype.wire_name()}, its workspace slot is "
+                                f"{out.dtype().wire_name()}")
+        if len(out) != n:
+            raise ShapeMismatch(f"graph.call: node {node.id!r} produces {n} elements, its workspace slot holds "
+                                f"{len(out)}")
+
+    def _cast(self, node: GraphNode, args: list[DeviceTensor], stream, out: DeviceTensor | None) -> DeviceTensor:
         if len(args) != 1:
             raise InvalidArgument(f"typer: shape.cast needs one input (node {node.id!r} has {len(args)})")
         x = args[0]
@@ -291,11 +521,22 @@ class GraphBackend:
             raise DTypeMismatch(f"shape.cast {node.id!r}: from_dtype {src.wire_name()} but the input is "
                                 f"{x.dtype().wire_name()}")
         target = cast_target(node, x.dtype())
+        if out is None:
+            if target == x.dtype():
+                return x
+            return self.backend.convert(x, target, compat=self.compat, stream=stream)
+        self._check_out(node, out, target, len(x))
         if target == x.dtype():
-            return x
-        return self.backend.convert(x, target, compat=self.compat, stream=stream)
+            if out.dispatch_pointer() != x.dispatch_pointer() and x.nbytes():
+                call("mf_memcpy_d2d_async", out.dispatch_pointer(), x.dispatch_pointer(), x.nbytes(),
+                     stream_handle(stream))
+            return out
+        if x.dtype() not in DECODE_SOURCES:
+            raise DTypeUnsupported(f"convert: unsupported source dtype {x.dtype().name}")
+        convert_raw(x.dtype(), target, x.dispatch_pointer(), out.dispatch_pointer(), len(x), self.compat, stream)
+        return out
 
-    def _fusion(self, node: GraphNode, args: list[DeviceTensor], stream) -> DeviceTensor:
+    def _fusion(self, node: GraphNode, args: list[DeviceTensor], stream, out: DeviceTensor | None) -> DeviceTensor:
         ks = node.attributes.get(KERNEL_ATTRIBUTE)
         kernel = ks.for_target(Target.CUDA) if isinstance(ks, KernelSet) else None
         if not isinstance(kernel, CUDAKernel):
@@ -319,6 +560,9 @@ class GraphBackend:
         for a, bc in zip(args, kernel.in_bcast):
             if not bc and len(a) != n:
                 raise InvalidArgument(f"fusion {node.id!r}: inputs of {len(a)} and {n} elements")
-        out = self.backend.empty(shape, kernel.out_dtype)
+        if out is None:
+            out = self.backend.empty(shape, kernel.out_dtype)
+        else:
+            self._check_out(node, out, kernel.out_dtype, n)
         kernel.run([a.dispatch_pointer() for a in args], out.dispatch_pointer(), n, stream=stream)
         return out

@@ -10,7 +10,7 @@
 // counted on an mbarrier), kStages tiles ahead of the consumers; all 256
 // threads decode the staged tile from shared memory, compute, and write the
 // result with 128-bit streaming stores.  The copy engine keeps up to
-// kStages x 3 CTAs x tile bytes of reads in flight per SM without any
+// kStages x (2 or 3) CTAs x tile bytes of reads in flight per SM without any
 // register cost, and the loads of later tiles overlap the compute of the
 // current one.
 //
@@ -33,7 +33,7 @@ namespace mf {
 constexpr int kStreamThreads = 256;
 constexpr int kConsumerWarps = kStreamThreads / 32;
 constexpr int64_t kTileElems = 8192;            // elements per tile
-constexpr int kStreamSmemBudget = 64 * 1024;    // staging bytes per CTA (3 CTAs per SM)
+constexpr int kStreamSmemBudget = 64 * 1024;    // staging bytes per CTA (room for 3 CTAs per SM)
 constexpr uint32_t kMbarSpinLimit = 1u << 24;   // polls of try_wait before giving up
 constexpr int kDeviceTimeout = MF_DEVICE_TIMEOUT;  // sticky status code of a timed-out wait
 
@@ -183,7 +183,17 @@ struct FixQueue {
     float4* v;    // this warp's slots: slot i holds a parked step's values in v[2i] (and v[2i+1] for 8 elements)
     uint8_t** d;  // and where its codes go
     uint32_t n;   // filled slots (warp-uniform)
+    uint32_t age; // tile ends passed since the oldest parked step (warp-uniform)
 };
+
+// When a tile ends, the warp drains its queue once it holds kDrainSlots steps or
+// its oldest step has waited kDrainTiles tiles.  Batching several tiles' fix-ups
+// into one drain halves their cost on activations (about half of all warp steps
+// park one lane there); the age bound keeps every parked store within a few tiles
+// of its neighbours, while their lines are still in L2 (on weights, where steps
+// park rarely, draining only when full measured slower).
+constexpr uint32_t kDrainSlots = 16;
+constexpr uint32_t kDrainTiles = 4;
 
 // Warp-collective: encode and store every parked step.
 template <class Op>
@@ -193,6 +203,7 @@ __device__ __forceinline__ void fix_drain(FixQueue& fq) {
     if (lane < fq.n) Op::fix(fq.v[2 * lane], fq.v[2 * lane + 1], fq.d[lane]);
     __syncwarp();
     fq.n = 0;
+    fq.age = 0;
 }
 
 // Warp-collective (all 32 lanes): park this lane's step when `fix` is set.
@@ -438,6 +449,7 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
     fq.d = reinterpret_cast<uint8_t**>(smem + G::kFixOffset + kConsumerWarps * kFixSlots * 32) +
            (threadIdx.x >> 5) * kFixSlots;
     fq.n = 0;
+    fq.age = 0;
     int k = stream_first_chunk(a, t0);
     typename Op::State st = Op::setup(a, a.chunk[k]);
     for (int64_t i = 0; i < ntiles; ++i) {
@@ -469,11 +481,9 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
                     const int q = threadIdx.x + j * kStreamThreads;
                     Op::template step<Op::kDefers>(tp + q * Op::kLane * Op::kIn, ch, e0 + Op::kLane * q, st, fq);
                 }
-                // fill the holes parked steps left in this tile's output while its
-                // lines are still in L2 (measured faster than letting the queue
-                // fill over several tiles)
+                // fill the holes parked steps left in recent tiles' output
                 if constexpr (Op::kDefers)
-                    if (fq.n) fix_drain<Op>(fq);
+                    if (fq.n && (fq.n >= kDrainSlots || ++fq.age >= kDrainTiles)) fix_drain<Op>(fq);
             } else {
                 const int copied = static_cast<int>(((cnt * Op::kIn) & ~int64_t(15)) / Op::kIn);
                 const int nsteps = copied / Op::kLane;

@@ -57,7 +57,7 @@ bool is_vector_format(int dt) {
 template <int SRC, int DST>
 cudaError_t launch_vec(const void* src, void* dst, int64_t n, int compat, cudaStream_t s) {
     StreamArgs<1> a{};
-    single_chunk(a, src, dst, n, true);
+    single_chunk(a, src, dst, n, true, stream_tile_elems<dtype_bytes(SRC)>());
     if (compat) return launch_stream<ConvertOp<SRC, DST, 1>, 1>(a, state().sm_count, s);
     return launch_stream<ConvertOp<SRC, DST, 0>, 1>(a, state().sm_count, s);
 }

@@ -15,7 +15,7 @@
 // current one.
 //
 // Work is a table of chunks (ChunkRec: src, dst, n, tensor); chunks are cut
-// into tiles of kTileElems elements and every CTA walks a contiguous range
+// into tiles of stream_tile_elems<source bytes>() elements and every CTA walks a contiguous range
 // of tiles (few chunk changes per CTA).  A chunk whose src or dst is not
 // 16-byte aligned is processed with plain loads (the producer arrives on the
 // stage barrier without a copy).  Ragged chunk ends (n not a multiple of 16)
@@ -32,7 +32,17 @@ namespace mf {
 
 constexpr int kStreamThreads = 256;
 constexpr int kConsumerWarps = kStreamThreads / 32;
-constexpr int64_t kTileElems = 8192;            // elements per tile
+// Elements per tile for a source format of InBytes bytes per element: 16384
+// for 1- and 2-byte formats (16 or 32 KB of source, 4 or 2 stages), 8192 for
+// 4-byte ones (32 KB, 2 stages).  A thread meets 8 or 16 lane steps per tile,
+// so the per-tile hand-off (mbarrier wait, chunk bookkeeping, fix-up check) is
+// paid half as often as with 8192-element tiles: the BF16 checkpoint cast
+// measured 9% faster, the FP8 decodes neither faster nor slower, 4096-element
+// tiles 10-20% slower everywhere.
+template <int InBytes>
+constexpr int64_t stream_tile_elems() {
+    return InBytes >= 4 ? 8192 : 16384;
+}
 constexpr int kStreamSmemBudget = 64 * 1024;    // staging bytes per CTA (room for 3 CTAs per SM)
 constexpr uint32_t kMbarSpinLimit = 1u << 24;   // polls of try_wait before giving up
 constexpr int kDeviceTimeout = MF_DEVICE_TIMEOUT;  // sticky status code of a timed-out wait
@@ -350,6 +360,7 @@ struct CastOp {
 
 template <class Op>
 struct StreamGeometry {
+    static constexpr int64_t kTileElems = stream_tile_elems<Op::kIn>();
     static constexpr int kTileBytes = static_cast<int>(kTileElems) * Op::kIn;
     static constexpr int kStages = (kStreamSmemBudget / kTileBytes) < 8 ? (kStreamSmemBudget / kTileBytes) : 8;
     static constexpr int kFixOffset = kStages * kTileBytes + kStages * 16;  // 16-byte aligned
@@ -423,8 +434,8 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
             const int64_t t = t0 + i;
             kp = stream_find_chunk(a, t, kp);
             const ChunkRec& ch = a.chunk[kp];
-            const int64_t e0 = (t - ch.tile_begin) * kTileElems;
-            const int64_t cnt = min(kTileElems, ch.n - e0);
+            const int64_t e0 = (t - ch.tile_begin) * G::kTileElems;
+            const int64_t cnt = min(G::kTileElems, ch.n - e0);
             const uint32_t bytes = static_cast<uint32_t>((cnt * Op::kIn) & ~int64_t(15));
             if (ch.aligned && bytes > 0) {
                 mbar_arrive_expect_tx(&full[s], bytes);
@@ -455,14 +466,14 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
     for (int64_t i = 0; i < ntiles; ++i) {
         const int64_t t = t0 + i;
         const int s = static_cast<int>(i % G::kStages);
-        if (a.chunk[k].tile_begin + ((a.chunk[k].n + kTileElems - 1) / kTileElems) <= t) {
+        if (a.chunk[k].tile_begin + ((a.chunk[k].n + G::kTileElems - 1) / G::kTileElems) <= t) {
             k = stream_find_chunk(a, t, k);
             st = Op::setup(a, a.chunk[k]);
         }
         const ChunkRec& ch = a.chunk[k];
         const int64_t tile = t - ch.tile_begin;
-        const int64_t e0 = tile * kTileElems;
-        const int64_t cnt = min(kTileElems, ch.n - e0);
+        const int64_t e0 = tile * G::kTileElems;
+        const int64_t cnt = min(G::kTileElems, ch.n - e0);
         // warp-uniform outcome: the lanes meet again in warp-collective fix-up code
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], static_cast<uint32_t>((i / G::kStages) & 1)))) {
             if (lane == 0) atomicExch(a.status, kDeviceTimeout);
@@ -473,9 +484,9 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
             // only the first ((cnt * kIn) & ~15) bytes were copied (16-byte
             // granularity); the elements past them come from global memory
             const uint8_t* tp = smem + s * G::kTileBytes;
-            if (cnt == kTileElems) {
+            if (cnt == G::kTileElems) {
                 // full tile: a fixed trip count, unrolled
-                constexpr int kStepsPerThread = static_cast<int>(kTileElems / Op::kLane / kStreamThreads);
+                constexpr int kStepsPerThread = static_cast<int>(G::kTileElems / Op::kLane / kStreamThreads);
 #pragma unroll
                 for (int j = 0; j < kStepsPerThread; ++j) {
                     const int q = threadIdx.x + j * kStreamThreads;
@@ -539,8 +550,8 @@ inline cudaError_t launch_stream(const StreamArgs<MaxChunks>& a, int sm_count, c
     return cudaGetLastError();
 }
 
-// One flat array as a single-chunk argument block.
-inline void single_chunk(StreamArgs<1>& a, const void* src, void* dst, int64_t n, bool aligned) {
+// One flat array as a single-chunk argument block, cut into tiles of tile_elems.
+inline void single_chunk(StreamArgs<1>& a, const void* src, void* dst, int64_t n, bool aligned, int64_t tile_elems) {
     a.chunk[0].src = src;
     a.chunk[0].dst = dst;
     a.chunk[0].n = n;
@@ -548,7 +559,7 @@ inline void single_chunk(StreamArgs<1>& a, const void* src, void* dst, int64_t n
     a.chunk[0].tensor = 0;
     a.chunk[0].aligned = aligned ? 1 : 0;
     a.n_chunks = 1;
-    a.total_tiles = (n + kTileElems - 1) / kTileElems;
+    a.total_tiles = (n + tile_elems - 1) / tile_elems;
     a.status = sticky_status_ptr();
 }
 

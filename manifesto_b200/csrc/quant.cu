@@ -219,7 +219,7 @@ void amax_dispatch(const void* src, int64_t n, float* d_amax, cudaStream_t s) {
 template <int SRC, int FP8>
 cudaError_t cast_dispatch(const void* src, void* dst, int64_t n, const float* d_amax, int compat, cudaStream_t s) {
     StreamArgs<1> a{};
-    single_chunk(a, src, dst, n, aligned16(src) && aligned16(dst));
+    single_chunk(a, src, dst, n, aligned16(src) && aligned16(dst), stream_tile_elems<dtype_bytes(SRC)>());
     a.amax = d_amax;
     if (compat) return launch_stream<CastOp<SRC, FP8, 1>, 1>(a, state().sm_count, s);
     return launch_stream<CastOp<SRC, FP8, 0>, 1>(a, state().sm_count, s);
@@ -354,7 +354,7 @@ int64_t fill_amax(AmaxArgs& a, const mf_chunk_desc* chunks, const int32_t* idx, 
 }
 
 int64_t fill_cast(StreamArgs<kGroupMaxChunks>& a, const mf_chunk_desc* chunks, const int32_t* idx, int first,
-                  int count) {
+                  int count, int64_t tile_elems) {
     int64_t tiles = 0;
     for (int i = 0; i < count; ++i) {
         const mf_chunk_desc& d = chunks[idx[first + i]];
@@ -365,7 +365,7 @@ int64_t fill_cast(StreamArgs<kGroupMaxChunks>& a, const mf_chunk_desc* chunks, c
         r.tile_begin = tiles;
         r.tensor = d.tensor;
         r.aligned = (aligned16(d.src) && aligned16(d.dst)) ? 1 : 0;
-        tiles += (d.n + kTileElems - 1) / kTileElems;
+        tiles += (d.n + tile_elems - 1) / tile_elems;
     }
     a.n_chunks = count;
     a.total_tiles = tiles;
@@ -535,7 +535,7 @@ int cast_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, 
         const int count = std::min<int>(kGroupMaxChunks, static_cast<int>(idx.size()) - first);
         args.amax = d_amax;
         args.status = sticky_status_ptr();
-        const int64_t tiles = fill_cast(args, chunks, idx.data(), first, count);
+        const int64_t tiles = fill_cast(args, chunks, idx.data(), first, count, stream_tile_elems<dtype_bytes(SRC)>());
         if (tiles == 0) continue;
         const cudaError_t err = (fp8_dtype == MF_DT_F8E4M3) ? cast_launch<SRC, MF_DT_F8E4M3>(args, compat, s)
                                                             : cast_launch<SRC, MF_DT_F8E5M2>(args, compat, s);
@@ -702,7 +702,7 @@ int noalloc_cast_launches(const mf_chunk_desc* chunks, int32_t n_chunks, const f
             r.tile_begin = tiles;
             r.tensor = d.tensor;
             r.aligned = (aligned16(d.src) && aligned16(d.dst)) ? 1 : 0;
-            tiles += (d.n + kTileElems - 1) / kTileElems;
+            tiles += (d.n + stream_tile_elems<dtype_bytes(SRC)>() - 1) / stream_tile_elems<dtype_bytes(SRC)>();
         }
         if (count == 0) continue;
         args.amax = d_amax;

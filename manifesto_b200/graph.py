@@ -421,8 +421,13 @@ class GraphBackend:
 
     def _stage_inputs(self, request: GraphCallRequest, ws: AttachedWorkspace | None, bindings: dict[str, int],
                       stream) -> dict[str, DeviceTensor]:
+        """Copy each input into its workspace slot.  An input that already lies in the arena
+        (an output of an earlier call fed back) and is not exactly its own slot is first
+        copied out, before any slot is written: its bytes may overlap its own slot or
+        another input's."""
         g = request.graph
         values: dict[str, DeviceTensor] = {}
+        plan: list[tuple[str, DeviceTensor, _Slot, tuple[int, ...], int]] = []
         for name in g.inputs:
             if name not in request.inputs:
                 raise InvalidArgument(f"graph.call {request.graph_name!r}: missing input {name!r}")
@@ -438,9 +443,28 @@ class GraphBackend:
             if t.nbytes() != nbytes:
                 raise ShapeMismatch(f"graph.call {request.graph_name!r}: input {name!r} holds {t.nbytes()} bytes, "
                                     f"the plan's {list(shape)} x {slot.dtype.wire_name()} is {nbytes}")
-            if t.dispatch_pointer() != slot.ptr and nbytes:
-                call("mf_memcpy_d2d_async", slot.ptr, t.dispatch_pointer(), nbytes, stream_handle(stream))
-            values[name] = DeviceTensor(self.backend, shape, slot.dtype, DeviceView(slot.ptr, nbytes))
+            plan.append((name, t, slot, shape, nbytes))
+        h = stream_handle(stream)
+        temps: list[DeviceBuffer] = []
+        try:
+            sources = {}
+            for name, t, slot, _, nbytes in plan:
+                src = t.dispatch_pointer()
+                if nbytes and src != slot.ptr and ws.contains(src):
+                    tmp = DeviceBuffer(nbytes)
+                    temps.append(tmp)
+                    call("mf_memcpy_d2d_async", tmp.ptr, src, nbytes, h)
+                    src = tmp.ptr
+                sources[name] = src
+            for name, t, slot, shape, nbytes in plan:
+                if sources[name] != slot.ptr and nbytes:
+                    call("mf_memcpy_d2d_async", slot.ptr, sources[name], nbytes, h)
+                values[name] = DeviceTensor(self.backend, shape, slot.dtype, DeviceView(slot.ptr, nbytes))
+        finally:
+            if temps:
+                call("mf_stream_sync", h)
+                for tmp in temps:
+                    tmp.free()
         return values
 
     def _call(self, request: GraphCallRequest, values: dict[str, DeviceTensor], stream_for, after, sync=(),

@@ -140,3 +140,43 @@ def test_pass_through_cast_copies_into_its_slot(backend):
     assert backend.download(out)[1] == x.tobytes()
     xt.close()
     gb.close()
+
+
+def test_inputs_that_live_in_the_arena(backend, ref):
+    """An output fed back as the next call's input: one that is exactly the input's slot
+    needs no copy; one that straddles the slot is copied out before the slot is written."""
+    from manifesto_b200._abi import call
+    from manifesto_b200.backend import DeviceTensor, DeviceView
+    n = 4096
+    bf, hf = T(DType.BFLOAT16, n), T(DType.FLOAT16, n)
+    g = graph.Graph(nodes=[
+        graph.GraphNode("a", graph.SHAPE_CAST, ["x"], {"dtype": "F16"}, input_types=[bf], output_type=hf),
+        graph.GraphNode("b", graph.SHAPE_CAST, ["a"], {"dtype": "BF16"}, input_types=[hf], output_type=bf),
+    ], inputs=["x"], outputs={"b": "b"})
+    gb = graph.GraphBackend(backend)
+    topo = gb.attach_workspace("loop", g)
+    ws = gb.workspace("loop")
+    # a@0, x@2n, b reuses x's slot once x is dead; the arena is 4n bytes
+    assert topo.input_ports == {"x": 2 * n} and topo.output_ports == {"b": 2 * n} and topo.workspace.size == 4 * n
+
+    def round_trip(v):
+        return ref.convert(ref.convert(v, BF16, F16).view(np.uint16), F16, BF16).view(np.uint16)
+
+    x = synthetic.normal_bf16(901, n, 0.0, 50.0)
+    xt = backend.upload([n], DType.BFLOAT16, x)
+    out = gb.call_graph(graph.GraphCallRequest("loop", g, {"x": xt})).outputs["b"]
+    assert out.dispatch_pointer() == ws.input_slots["x"].ptr
+    want = round_trip(x)
+    assert np.array_equal(host(backend, out, np.uint16), want)
+    out = gb.call_graph(graph.GraphCallRequest("loop", g, {"x": out})).outputs["b"]   # its own slot
+    want = round_trip(want)
+    assert np.array_equal(host(backend, out, np.uint16), want)
+    # the same values placed across a's slot and x's slot
+    straddle = ws.base + 2 * n - 256
+    call("mf_memcpy_d2d_async", straddle, xt.dispatch_pointer(), 2 * n, None)
+    call("mf_stream_sync", None)
+    view = DeviceTensor(backend, (n,), DType.BFLOAT16, DeviceView(straddle, 2 * n))
+    out = gb.call_graph(graph.GraphCallRequest("loop", g, {"x": view})).outputs["b"]
+    assert np.array_equal(host(backend, out, np.uint16), round_trip(x))
+    xt.close()
+    gb.close()

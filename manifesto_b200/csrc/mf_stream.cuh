@@ -185,8 +185,8 @@ __device__ __forceinline__ void load_decode_lane(const uint8_t* sp, float (&v)[2
 // fixing it inline makes the whole warp run the fix-up.  Instead each warp
 // parks the lane steps that need it in a 32-slot shared-memory queue (ballot
 // + prefix count; the lane skips its store) and encodes the parked steps
-// together, one per lane, at the end of each tile (or when the queue is
-// full).  A slot keeps its destination address.
+// together, one per lane, at a tile end (see kDrainSlots / kDrainTiles) or
+// when the queue is full.  A slot keeps its destination address.
 constexpr int kFixSlots = 32;
 
 struct FixQueue {

@@ -233,3 +233,25 @@ def test_lowest_gap_is_reused():
     total, out = wsp.allocate_offsets(ivs, 64)
     assert [iv.offset for iv in out] == [0, 128, 192, 128, 256] and total == 384
     assert [iv.size for iv in out] == [128, 64, 64, 64, 128]
+
+
+def test_diamond_hazards_under_a_stream_schedule():
+    """a = f(x); b, c = g(a), h(a); d = k(b, c); e = m(y) with N-element F32/F16/BF16/E4M3 ports.
+    e's output is given a's bytes (and d's): e runs on its own stream, so it must wait for
+    every node that touched them; d is a graph output that e overwrites."""
+    from manifesto_b200.graph import schedule_streams
+    n = 1024
+    f32, f16, bf, q = (wsp.port_type(d, n) for d in (F32, DType.FLOAT16, DType.BFLOAT16, DType.FLOAT8_E4M3))
+    g = Graph([GraphNode("a", "shape.cast", ["x"], input_types=[bf], output_type=f32),
+               GraphNode("b", "shape.cast", ["a"], input_types=[f32], output_type=f16),
+               GraphNode("c", "shape.cast", ["a"], input_types=[f32], output_type=bf),
+               GraphNode("d", "optimizer.fusion", ["b", "c"], input_types=[f16, bf], output_type=f32),
+               GraphNode("e", "shape.cast", ["y"], input_types=[bf], output_type=q)],
+              ["x", "y"], {"d": "d", "e": "e"})
+    topo = wsp.plan_graph(g)
+    offs = [nd.outputs[0].allocation.base_offset for nd in topo.nodes]
+    # a@0 (4N), x@4N, y@6N, b@4N (x dead), c@8N, d@0 (a dead), e@0 (b, c, d dead)
+    assert offs == [0, 4 * n, 8 * n, 0, 0] and topo.input_ports == {"x": 4 * n, "y": 6 * n}
+    deps, snap = plan_hazards(g, topo)
+    assert deps == [(), (0,), (), (0, 1, 2), (0, 1, 2, 3)] and snap == {3}
+    assert [schedule_streams(g)[i].stream_id for i in "abcde"] == [0, 0, 1, 0, 2]

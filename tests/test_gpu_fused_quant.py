@@ -447,6 +447,35 @@ def test_ckpt_scale_inv_covers_tensors_without_local_elements(backend, ref):
         b.free()
 
 
+@pytest.mark.parametrize("fp8", [E4M3, E5M2])
+def test_ckpt_mixed_source_dtypes(backend, ref, fp8):
+    """One checkpoint call over BF16, F16 and F32 tensors: the library launches each source
+    dtype's chunks separately (F32 tiles hold 8192 elements, 16-bit ones 16384), sizes are
+    ragged, and two tensors are split into two chunks at an element offset that leaves the
+    second chunk off 16-byte alignment.  Codes and scale_inv are bit-exact against the oracle."""
+    specs = [(BF16, 40000), (F16, 33333), (F32, 20001), (BF16, 3 * 16384 + 5), (F32, 5 * 8192), (F16, 17)]
+    splits = {0: 12345, 2: 7}
+    wire = {BF16: DType.BFLOAT16, F16: DType.FLOAT16, F32: DType.FLOAT32}
+    raws, srcs, dsts, entries = [], [], [], []
+    for t, (dt, n) in enumerate(specs):
+        v = synthetic.normal_f32(800 + t, n, 0.0, 0.05 * (t + 1))
+        raw = v.view(np.uint32).copy() if dt == F32 else ref.convert(v, F32, dt)
+        src, dst = to_device(raw), empty(n)
+        raws.append(raw), srcs.append(src), dsts.append(dst)
+        cuts = [0, splits[t], n] if t in splits else [0, n]
+        for a, b in zip(cuts, cuts[1:]):
+            entries.append((src.ptr + a * ITEMSIZE[dt], dst.ptr + a, b - a, t, wire[dt]))
+    am, si = empty(4 * len(specs)), empty(4 * len(specs))
+    checkpoint.quantise(checkpoint.make_chunks(entries), len(entries), len(specs), am.ptr, si.ptr, DType(fp8))
+    got_si = fetch(si, 4 * len(specs), np.float32)
+    for t, ((dt, n), raw) in enumerate(zip(specs, raws)):
+        a = ref.amax(raw, dt)
+        assert float(got_si[t]) == ref.fp8_scale_inv(a, fp8), t
+        bits_equal(fetch(dsts[t], n), ref.scaled_cast(raw, dt, fp8, a))
+    for b in srcs + dsts + [am, si]:
+        b.free()
+
+
 def test_ckpt_quantise_from_several_host_threads(backend, ref):
     """cgo may call from any OS thread: four threads quantise four checkpoints at once, each on
     its own stream, through the grouped launches that share the library's argument blocks."""

@@ -17,8 +17,9 @@
 //
 // Checkpoint quantisation: each rank owns one contiguous chunk of every
 // tensor.  One descriptor table (passed by value as the kernel parameter,
-// so nothing is allocated) lists the chunks; the chunks are cut into
-// 16384-element tiles and each CTA walks a contiguous range of tiles, so a
+// so nothing is allocated) lists the chunks; the chunks are cut into tiles
+// (16384 elements of a 16-bit source, 8192 of a float32 one) and each CTA
+// walks a contiguous range of tiles, so a
 // CTA crosses few tensor boundaries and reduces its per-tensor maximum
 // once per crossing.  Pass 1 (amax) and pass 2 (cast) are one launch each
 // per 512 chunks; between them an NCCL max all-reduce of the amax vector

@@ -356,11 +356,27 @@ int mf_ckpt_quant_fp8(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_t
  * held until the process exits); larger n_tensors return
  * MF_ERR_ALLOCATOR_EXHAUSTED.  Nothing is allocated.  Every call on a device
  * shares that array, so calls that overlap on the GPU race; each call zeroes
- * the entries it uses.  The first call on a device looks the array up with
- * that device current; make it before any stream capture. */
+ * the entries it uses.  Every call looks the array's device address up with
+ * the library's device current (nothing is cached, so a context the host
+ * tears down and creates again is safe); the first call on a device also
+ * loads the array there, so make it before any stream capture. */
 int mf_ckpt_quant_fp8_noalloc(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors,
                               float* d_scale_inv, int fp8_dtype, int compat, mf_comm comm,
                               mf_stream stream);
+
+/* ---------------------------------------------------------------------
+ * Measurement.  No counterpart in the reference (it has no device code).
+ * mf_bw_probe moves bytes in a fixed read:write mix with the access forms of
+ * the kernels above (16-byte evict-first loads, 16-byte streaming stores)
+ * and does no other work; its rate is the DRAM ceiling of that mix, the
+ * denominator for a kernel with the same mix.  One step reads in_per_step
+ * 16-byte vectors (read k of step s at src + 16 * (k * n_steps + s)) and
+ * writes out_per_step (same layout in dst).  Mixes: (1,0) read-only,
+ * (0,1) write-only, (1,1) copy, (1,4) decode-shaped, (2,1) cast-shaped.
+ * A read-only probe needs d_sink (one uint32_t, written only in a case no
+ * data produces).  Buffers 16-byte aligned. */
+int mf_bw_probe(const void* src, int in_per_step, void* dst, int out_per_step, int64_t n_steps,
+                uint32_t* d_sink, mf_stream stream);
 
 #ifdef __cplusplus
 }

@@ -99,6 +99,7 @@ SIGNATURES: dict[str, list] = {
     "mf_ckpt_cast_pass": [ctypes.POINTER(ChunkDesc), _i32, _i32, _vp, _vp, _int, _int, _vp],
     "mf_ckpt_quant_fp8": [ctypes.POINTER(ChunkDesc), _i32, _i32, _vp, _vp, _int, _int, _vp, _vp],
     "mf_ckpt_quant_fp8_noalloc": [ctypes.POINTER(ChunkDesc), _i32, _i32, _vp, _int, _int, _vp, _vp],
+    "mf_bw_probe": [_vp, _int, _vp, _int, _i64, _vp, _vp],
 }
 
 _lib: ctypes.CDLL | None = None

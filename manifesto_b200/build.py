@@ -31,6 +31,7 @@ SOURCES = [
     "quant.cu",
     "fused.cu",
     "comm.cu",
+    "probe.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

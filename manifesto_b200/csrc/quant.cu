@@ -622,9 +622,12 @@ extern "C" int mf_ckpt_quant_fp8(const mf_chunk_desc* chunks, int32_t n_chunks, 
 //     exits, and every call on a device shares it: calls that overlap on the
 //     GPU (on streams with no ordering between them) race on it.
 //   * Each call zeroes the entries it uses before pass 1.
-//   * The first call on each device looks up the array's device address with
-//     cudaGetSymbolAddress, with that device current; make that first call
-//     before any stream capture begins.
+//   * Every call looks up the array's device address with
+//     cudaGetSymbolAddress, with the library's device current (no address is
+//     kept between calls, so a context torn down and made again by the host
+//     never leaves a stale one).  The first call on a device also loads the
+//     module's device globals there; make that first call before any stream
+//     capture begins.
 //   * Nothing is allocated: no cudaMalloc/cudaFree and no host heap use (the
 //     chunk table is scanned in place instead of being grouped into lists).
 namespace mf {
@@ -632,23 +635,12 @@ namespace {
 
 constexpr int kNoAllocMaxTensors = 4096;
 __device__ __align__(256) float g_noalloc_amax[kNoAllocMaxTensors];
-constexpr int kNoAllocMaxDevices = 64;
-float* g_noalloc_amax_addr[kNoAllocMaxDevices] = {};  // device address of the array, per device
-std::mutex g_noalloc_setup_mutex;
 
 int noalloc_scratch(float** out) {
-    int dev = 0;
-    MF_CUDA_CHECK(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= kNoAllocMaxDevices)
-        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_quant_fp8_noalloc: device %d out of range", dev);
-    std::lock_guard<std::mutex> lock(g_noalloc_setup_mutex);
-    if (!g_noalloc_amax_addr[dev]) {
-        void* p = nullptr;
-        const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_amax);
-        if (err != cudaSuccess) return cuda_fail(err, "mf_ckpt_quant_fp8_noalloc: cudaGetSymbolAddress");
-        g_noalloc_amax_addr[dev] = static_cast<float*>(p);
-    }
-    *out = g_noalloc_amax_addr[dev];
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_amax);
+    if (err != cudaSuccess) return cuda_fail(err, "mf_ckpt_quant_fp8_noalloc: cudaGetSymbolAddress");
+    *out = static_cast<float*>(p);
     return MF_OK;
 }
 

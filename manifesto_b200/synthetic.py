@@ -33,10 +33,13 @@ def uniform_bytes(seed: int, n: int) -> np.ndarray:
     return words.view(np.uint8)[:n].copy()
 
 
-def normal_f32(seed: int, n: int, mu: float = 0.0, sigma: float = 1.0) -> np.ndarray:
-    """N(mu, sigma) float32 values by Box-Muller in float64."""
+def normal_f32(seed: int, n: int, mu: float = 0.0, sigma: float = 1.0, offset: int = 0) -> np.ndarray:
+    """N(mu, sigma) float32 values by Box-Muller in float64: elements offset .. offset+n-1 of the
+    stream (offset even; value 2j and 2j+1 come from stream words 2j and 2j+1)."""
+    if offset % 2:
+        raise ValueError("normal_f32: offset must be even")
     m = (n + 1) // 2
-    w = splitmix64(seed, 2 * m)
+    w = splitmix64(seed, 2 * m, offset)
     u1 = ((w[0::2] >> np.uint64(11)).astype(np.float64) + 1.0) * (1.0 / 9007199254740992.0)  # (0, 1]
     u2 = (w[1::2] >> np.uint64(11)).astype(np.float64) * (1.0 / 9007199254740992.0)
     r = np.sqrt(-2.0 * np.log(u1))
@@ -59,3 +62,19 @@ def normal_bf16(seed: int, n: int, mu: float = 0.0, sigma: float = 1.0) -> np.nd
 
 def abs_normal_bf16(seed: int, n: int, sigma: float) -> np.ndarray:
     return f32_to_bf16_bits(np.abs(normal_f32(seed, n, 0.0, sigma)))
+
+
+def normal_bf16_large(seed: int, n: int, mu: float = 0.0, sigma: float = 1.0, piece: int = 1 << 24,
+                      threads: int = 8) -> np.ndarray:
+    """normal_bf16(seed, n, mu, sigma), generated in pieces on a thread pool (the float64
+    temporaries of one 500M-element call would need ~15 GB)."""
+    from concurrent.futures import ThreadPoolExecutor
+    out = np.empty(n, dtype=np.uint16)
+
+    def fill(a: int) -> None:
+        b = min(n, a + piece)
+        out[a:b] = f32_to_bf16_bits(normal_f32(seed, b - a, mu, sigma, offset=a))
+
+    with ThreadPoolExecutor(max(1, threads)) as ex:
+        list(ex.map(fill, range(0, n, piece)))
+    return out

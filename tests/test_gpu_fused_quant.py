@@ -241,6 +241,48 @@ def test_fused_fp8_pipeline(backend, ref):
         b.free()
 
 
+def test_fused_fp8_pipeline_config4_full_size(backend, ref):
+    """Config 4 at its stated size, BF16 [64, 2048, 4096] = 2^29 elements, through the same call the
+    benchmark times (CUDAKernel.run_fp8): every pre-cast value within 1 BF16 ulp of evalCPU's
+    restatement, every FP8 code within 1 code of the oracle's pipeline, the FP8 codes bit-exact under
+    the oracle's cast of the GPU's own pre-cast values, and amax / scale_inv exact.  x, y ~ N(0, 1),
+    gamma ~ N(1, 0.1), beta ~ N(0, 0.1), drawn on the device and checked on the host."""
+    torch = pytest.importorskip("torch")
+    hidden, n = 4096, 64 * 2048 * 4096
+    gen = torch.Generator(device="cuda").manual_seed(4040)
+    x = torch.empty(n, dtype=torch.bfloat16, device="cuda").normal_(0.0, 1.0, generator=gen)
+    y = torch.empty(n, dtype=torch.bfloat16, device="cuda").normal_(0.0, 1.0, generator=gen)
+    g = torch.empty(hidden, dtype=torch.bfloat16, device="cuda").normal_(1.0, 0.1, generator=gen)
+    b = torch.empty(hidden, dtype=torch.bfloat16, device="cuda").normal_(0.0, 0.1, generator=gen)
+    pre = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    q = torch.empty(n, dtype=torch.uint8, device="cuda")
+    am = torch.zeros(1, dtype=torch.float32, device="cuda")
+    si = torch.zeros(1, dtype=torch.float32, device="cuda")
+    f, k = swiglu_kernel(hidden)
+    assert k.specialised()
+    k.run_fp8([x.data_ptr(), g.data_ptr(), b.data_ptr(), y.data_ptr()], pre.data_ptr(), q.data_ptr(), n,
+              am.data_ptr(), si.data_ptr())
+    torch.cuda.synchronize()
+    host = lambda t: t.view(torch.int16).cpu().numpy().view(np.uint16)
+    ins = [host(x), host(g), host(b), host(y)]
+    got_pre, got_q = host(pre), q.cpu().numpy()
+    got_amax, got_si = float(am.item()), float(si.item())
+    del x, y, pre, q
+    torch.cuda.empty_cache()
+    th = host_threads()
+    want_pre = ref.fused_eval(fusion.node_table(f.root), ins, [BF16] * 4, [0, hidden, hidden, 0], BF16, n, threads=th)
+    step = 1 << 26  # compare in slices: the int64 distance arrays of 2^29 elements would take ~25 GB
+    assert max(int(ulp_diff_16(got_pre[i:i + step], want_pre[i:i + step]).max()) for i in range(0, n, step)) <= 1
+    want_amax = ref.amax(want_pre, BF16, threads=th)
+    want_q = ref.scaled_cast(want_pre, BF16, E4M3, want_amax, threads=th)
+    assert max(int(ulp_diff_fp8(got_q[i:i + step], want_q[i:i + step]).max()) for i in range(0, n, step)) <= 1
+    del want_pre, want_q
+    assert got_amax == ref.amax(got_pre, BF16, threads=th)
+    assert got_si == ref.fp8_scale_inv(got_amax, E4M3)
+    bits_equal(got_q, ref.scaled_cast(got_pre, BF16, E4M3, got_amax, threads=th))
+    k.close()
+
+
 # --------------------------------------------------------------- quant
 
 @pytest.mark.parametrize("dt", [F32, BF16, F16, E4M3, E5M2])

@@ -3,7 +3,9 @@
 One process per GPU; each quantises its row range of every tensor with
 mf_ckpt_quant_fp8 and the NCCL max all-reduce of the amax vector between the
 two passes.  The shards, put back together, must equal the CPU oracle's
-single-process quantisation bit for bit.  Skipped with fewer than 2 GPUs.
+single-process quantisation bit for bit; mf_ckpt_quant_fp8_noalloc over the
+same communicator must give the same bytes.  NCCL runs with its defaults, as
+in bench.py.  Skipped with fewer than 2 GPUs.
 """
 import os
 import socket
@@ -38,11 +40,10 @@ def _rank_main(rank: int, port: int, out_dir: str) -> None:
 
     import torch.distributed as dist
 
-    from manifesto_b200 import CUDABackend, checkpoint, sync_device
+    from manifesto_b200 import CUDABackend, _abi, checkpoint, sync_device
     from manifesto_b200.dtype import DType
     from tests.gpu_util import empty, fetch, to_device
 
-    os.environ["NCCL_NVLS_ENABLE"] = "0"
     CUDABackend(rank)
     store = dist.TCPStore("127.0.0.1", port, WORLD, rank == 0, timeout=datetime.timedelta(seconds=60))
     comm = checkpoint.Communicator.from_store(store, WORLD, rank)
@@ -60,8 +61,18 @@ def _rank_main(rank: int, port: int, out_dir: str) -> None:
     checkpoint.quantise(checkpoint.make_chunks(entries), len(entries), len(specs), am.ptr, si.ptr, comm=comm)
     sync_device()
     out = [fetch(d, n) for d, n in zip(dsts, sizes)]
+    # the allocation-free entry point over the same communicator: the same codes and scales
+    na_dsts = [empty(n) for n in sizes]
+    na_si = empty(4 * len(specs))
+    na_entries = [(e[0], d.ptr, e[2], e[3], e[4]) for e, d in zip(entries, na_dsts)]
+    rc = _abi.lib().mf_ckpt_quant_fp8_noalloc(checkpoint.make_chunks(na_entries), len(na_entries), len(specs),
+                                              na_si.ptr, int(DType.FLOAT8_E4M3), 0, comm.handle, None)
+    assert rc == 0, _abi.last_error()
+    sync_device()
+    noalloc_same = all(np.array_equal(fetch(d, n), o) for d, n, o in zip(na_dsts, sizes, out)) and np.array_equal(
+        fetch(na_si, 4 * len(specs)), fetch(si, 4 * len(specs)))
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), amax=fetch(am, 4 * len(specs), np.float32),
-             scale_inv=fetch(si, 4 * len(specs), np.float32), *out)
+             scale_inv=fetch(si, 4 * len(specs), np.float32), noalloc_same=np.array([noalloc_same]), *out)
     comm.close()
 
 
@@ -85,6 +96,7 @@ def test_two_gpu_nccl_quantisation(backend, ref, tmp_path):
         full = _tensor(t, s)
         want_amax = ref.amax(full, ref.BF16)
         for r in range(WORLD):
+            assert bool(res[r]["noalloc_same"][0]), r
             assert res[r]["amax"][t] == want_amax, (s.name, r)
             assert res[r]["scale_inv"][t] == ref.fp8_scale_inv(want_amax, ref.E4M3)
         got = np.concatenate([res[r][f"arr_{t}"] for r in range(WORLD)])

@@ -4,26 +4,32 @@
 Headline workload (one JSON line on rank 0): whole-checkpoint FP8 E4M3
 quantisation of a Llama-3-8B layout (291 BF16 tensors, 8,030,261,248 params,
 values N(0, 0.02)) with per-tensor amax scales, every tensor row-split over the
-N ranks (strong scaling: the checkpoint is fixed), one NCCL max all-reduce of the
-amax vector per step.  A step = pass 1 (amax) + all-reduce + pass 2 (cast)
-through the C ABI (mf_ckpt_quant_fp8).
+N ranks (strong scaling: the checkpoint is fixed).  A step is one launch of the
+checkpoint plan (mf_ckpt_plan_run): per group of tensors an amax phase, the
+per-group amax exchanged between the ranks inside the kernel over NVLink peer
+memory, and a cast phase that re-reads the group from L2.  --path twopass times
+mf_ckpt_quant_fp8 instead (amax pass, NCCL max all-reduce, cast pass).
 
   value      params quantised per second, whole job (max-over-ranks device time)
   e2e        the same through the C ABI with host buffers: pinned host BF16 ->
-             device, quantise, FP8 + scales -> host, every step
-  roofline   the dominant kernel (pass 2, stream_kernel<CastOp>) timed alone with
-             CUDA events: 3 B/param (read BF16, write FP8) / launch time vs the
-             measured HBM copy peak
+             device, quantise, FP8 + scales -> host, every step, beside the bare
+             pinned-copy ceiling of the same bytes (link_ceiling_gbs)
+  roofline   the step's kernel timed alone with CUDA events: 3 B/param (BF16 read
+             once, E4M3 written once: the single-pass bound) / launch time vs the
+             measured HBM copy peak and vs the measured ceiling of its 2:1
+             read:write mix (mf_bw_probe)
+  two_pass   the two-pass path on the same buffers: each pass alone and the step's
+             phases (memset, pass 1, all-reduce, pass 2) with events between them,
+             max over ranks
   kernels    (N=1) every other benchmark config as its own kernel line: FP8->FP32
-             decode, Int4 group dequant, axpy f32/bf16, fused SwiGLU->FP8
+             decode, Int4 group dequant, axpy f32/bf16, fused SwiGLU->FP8, each with
+             the measured ceiling of its read:write mix
   cpu_baseline  (N=1, rank 0) the C oracle port of the Go loops on the host cores,
              on a bounded sample (the embedding matrix + decoder layer 0: 743,448,576
              params); each kernel line carries its own config's port timing under "cpu"
-  parity     (every N, after the timed region) the all-reduced amax vector against a
+  parity     (every N, after the timed region) the amax vector against a
              torch.distributed all-reduce of each rank's own max|v|, and four tensors'
              FP8 shards against the CPU oracle; exit status 3 on a mismatch
-  step_breakdown  the step's phases (memset, pass 1, all-reduce, pass 2) timed with
-             events between them, max over ranks
 
 --impl reference times that CPU port alone (the reference is Go; no Go toolchain
 exists on these machines, so the port stands in for it).
@@ -158,6 +164,13 @@ class Dist:
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
+    def all_gather_bytes(self, data: bytes) -> list[bytes]:
+        if not self.pg:
+            return [data]
+        out = [None] * self.world
+        self.pg.all_gather_object(out, data)
+        return out
+
     def broadcast_bytes(self, data: bytes | None) -> bytes:
         if not self.pg:
             return data
@@ -217,11 +230,10 @@ PROBE_MIXES = {(1, 0): "read-only", (0, 1): "write-only", (1, 1): "copy 1:1", (1
 
 def probe_ceiling(torch, stream_handle: int, src_ptr: int, a: int, dst_ptr: int, b: int, n_steps: int, flush=None,
                   reps: int = 20) -> dict:
-    """DRAM ceiling of one read:write mix, measured with mf_bw_probe (the library's own access forms,
-    no other work) on the given buffers: median of `reps` launches, L2 flushed before each."""
+    """DRAM ceiling of one read:write mix, measured with mf_bw_probe (bulk-copy loads and stores, no other
+    work) on the given buffers: median of `reps` launches, L2 flushed before each."""
     from manifesto_b200._abi import call
-    sink = torch.zeros(4, dtype=torch.int32, device="cuda")
-    f = lambda: call("mf_bw_probe", src_ptr, a, dst_ptr, b, n_steps, sink.data_ptr(), stream_handle)
+    f = lambda: call("mf_bw_probe", src_ptr, a, dst_ptr, b, n_steps, stream_handle)
     _warm(f)
     ms = statistics.median(time_launches(torch, f, reps, flush))
     nbytes = 16 * n_steps * (a + b)
@@ -398,10 +410,19 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
     if world > 1:
         uid = dist.broadcast_bytes(checkpoint.Communicator.unique_id() if rank == 0 else None)
         comm = checkpoint.Communicator(world, rank, uid)
+    plan = None
+    if args.path == "plan":
+        plan = checkpoint.QuantPlan(chunks, len(entries), len(specs), tensor_numel=[s.numel for s in specs],
+                                    group_bytes=int(args.group_mb * (1 << 20)), world=world, rank=rank)
+        plan.connect(dist.all_gather_bytes(plan.ipc_handle))
+        dist.barrier(torch)
 
     def step():
-        checkpoint.quantise(chunks, len(entries), len(specs), amax.data_ptr(), sinv.data_ptr(), E4M3, 0, comm,
-                            stream)
+        if plan is not None:
+            plan.run(amax.data_ptr(), sinv.data_ptr(), stream)
+        else:
+            checkpoint.quantise(chunks, len(entries), len(specs), amax.data_ptr(), sinv.data_ptr(), E4M3, 0, comm,
+                                stream)
 
     for _ in range(args.warmup):
         step()
@@ -421,9 +442,36 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
     local_ms = t0.elapsed_time(t1)
     ms = dist.max(torch, local_ms)
     value = total_params * args.steps / (ms * 1e-3)
-    job_gbs = 5.0 * total_params * args.steps / (ms * 1e-3) / 1e9
+    job_gbs = 3.0 * total_params * args.steps / (ms * 1e-3) / 1e9
 
-    # dominant kernel alone: pass 2 (stream_kernel<CastOp>), events around each launch
+    # the DRAM ceilings of the step's access mixes on this rank's buffers (the probes overwrite dst only)
+    ceilings = {"read_only": probe_ceiling(torch, stream, src.data_ptr(), 1, 0, 0, 2 * local_params // 16, reps=10),
+                "read2_write1": probe_ceiling(torch, stream, src.data_ptr(), 2, dst.data_ptr(), 1, local_params // 16,
+                                              reps=10)}
+    traffic = traffic_table()
+    one_pass_bytes = 3.0 * local_params  # read BF16 once, write E4M3 once: the single-pass lower bound
+    if plan is not None:
+        # the dominant (only) kernel: the one-launch step, events around each launch
+        run_ms = statistics.mean(time_launches(torch, step, 10))
+        achieved = one_pass_bytes / (run_ms * 1e-3) / 1e9
+        tr = traffic.get("ckpt_plan_kernel")
+        info = plan.info()
+        roofline = {"bound": "hbm", "kernel": "ckpt_plan_kernel<BF16,E4M3> (amax and cast phases per tensor group, "
+                                              "the cast phase re-reading its group from L2)",
+                    "alg_bytes_per_launch": int(one_pass_bytes),
+                    "alg_bytes_basis": "3 B/param: BF16 read once from DRAM + E4M3 written once (the single-pass "
+                                       "bound); the cast phase's second read of each group is served by L2",
+                    "launch_ms": round(run_ms, 4), "achieved": round(achieved, 1), "peak": peak,
+                    "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                    "frac_of_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
+                    "traffic": int(tr * local_params) if tr else None,
+                    "direction_ceiling": ceilings["read2_write1"],
+                    "frac_of_direction_ceiling": round(achieved / ceilings["read2_write1"]["gbs"], 4),
+                    "groups": info["groups"], "grid": info["grid"], "group_mb": args.group_mb}
+    # the two-pass path (mf_ckpt_quant_fp8: amax pass, NCCL all-reduce, cast pass) on the same buffers, for
+    # comparison: its phases and each pass alone
+    breakdown = step_breakdown(torch, dist, chunks, entries, specs, amax, sinv, comm, stream)
+
     def cast_only():
         call("mf_ckpt_cast_pass", chunks, len(entries), len(specs), amax.data_ptr(), sinv.data_ptr(), E4M3, 0,
              stream)
@@ -431,32 +479,28 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
     def amax_only():
         call("mf_ckpt_amax_pass", chunks, len(entries), len(specs), amax.data_ptr(), stream)
 
-    reps = 10
-    cast_ms = statistics.mean(time_launches(torch, cast_only, reps))
-    amax_ms = statistics.mean(time_launches(torch, amax_only, reps))
-    step()  # restore amax after the extra amax passes
-    torch.cuda.synchronize()
-    cast_bytes = 3.0 * local_params
-    achieved = cast_bytes / (cast_ms * 1e-3) / 1e9
-    traffic = traffic_table().get("ckpt_cast_pass")
-    roofline = {"bound": "hbm", "kernel": "stream_kernel<CastOp<BF16,E4M3>> (pass 2: read BF16, write E4M3)",
-                "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_src, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "frac_of_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
-                "traffic": int(traffic * local_params) if traffic else None,
-                "alg_bytes_per_launch": int(cast_bytes), "launch_ms": round(cast_ms, 4),
-                "amax_pass": {"launch_ms": round(amax_ms, 4),
-                              "gbs": round(2.0 * local_params / (amax_ms * 1e-3) / 1e9, 1)}}
-
-    # the step's phases, one event between each, and the DRAM ceilings of the passes' access mixes
-    breakdown = step_breakdown(torch, dist, chunks, entries, specs, amax, sinv, comm, stream)
-    ceilings = {"pass1_amax": probe_ceiling(torch, stream, src.data_ptr(), 1, 0, 0, 2 * local_params // 16, reps=10),
-                "pass2_cast": probe_ceiling(torch, stream, src.data_ptr(), 2, dst.data_ptr(), 1, local_params // 16,
-                                            reps=10)}
-    roofline["frac_of_direction_ceiling"] = round(achieved / ceilings["pass2_cast"]["gbs"], 4)
-    roofline["direction_ceiling"] = ceilings["pass2_cast"]
-    roofline["amax_pass"]["frac_of_direction_ceiling"] = round(
-        roofline["amax_pass"]["gbs"] / ceilings["pass1_amax"]["gbs"], 4)
-    roofline["amax_pass"]["direction_ceiling"] = ceilings["pass1_amax"]
+    cast_ms = statistics.mean(time_launches(torch, cast_only, 10))
+    amax_ms = statistics.mean(time_launches(torch, amax_only, 10))
+    cast_gbs = one_pass_bytes / (cast_ms * 1e-3) / 1e9
+    amax_gbs = 2.0 * local_params / (amax_ms * 1e-3) / 1e9
+    tr = traffic.get("ckpt_cast_pass")
+    two_pass = {"cast_pass": {"kernel": "stream_kernel<CastOp<BF16,E4M3>> (read BF16, write E4M3)",
+                              "launch_ms": round(cast_ms, 4), "gbs": round(cast_gbs, 1),
+                              "frac": round(cast_gbs / peak, 4),
+                              "frac_of_direction_ceiling": round(cast_gbs / ceilings["read2_write1"]["gbs"], 4),
+                              "traffic": int(tr * local_params) if tr else None},
+                "amax_pass": {"kernel": "group_amax_kernel<BF16> (read BF16)", "launch_ms": round(amax_ms, 4),
+                              "gbs": round(amax_gbs, 1), "frac": round(amax_gbs / peak, 4),
+                              "frac_of_direction_ceiling": round(amax_gbs / ceilings["read_only"]["gbs"], 4)},
+                "step": breakdown}
+    if plan is None:
+        roofline = {"bound": "hbm", "kernel": two_pass["cast_pass"]["kernel"], "alg_bytes_per_launch": int(one_pass_bytes),
+                    "launch_ms": round(cast_ms, 4), "achieved": round(cast_gbs, 1), "peak": peak,
+                    "peak_source": peak_src, "unit": "GB/s", "frac": round(cast_gbs / peak, 4),
+                    "frac_of_8tbs": round(cast_gbs / NOMINAL_HBM_GBS, 4),
+                    "traffic": int(tr * local_params) if tr else None,
+                    "direction_ceiling": ceilings["read2_write1"],
+                    "frac_of_direction_ceiling": round(cast_gbs / ceilings["read2_write1"]["gbs"], 4)}
 
     # the sharded result of one more step, checked outside the timed region
     step()
@@ -479,6 +523,9 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
 
     if comm is not None:
         comm.close()
+    if plan is not None:
+        dist.barrier(torch)  # every rank's last run has finished before any exchange buffer goes away
+        plan.close()
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "elems/s", "n_gpus": world, "steps": args.steps,
@@ -487,13 +534,18 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
             "config": {"workload": "ckpt_fp8_e4m3_llama3_8b" if full else
                        f"ckpt_fp8_e4m3_reduced_layers{args.ckpt_layers}_vocab{args.ckpt_vocab} (profiling size)",
                        "description": "whole-checkpoint per-tensor amax-scaled FP8 E4M3 quantisation, Llama-3-8B "
-                                      "layout (291 BF16 tensors), rows split over ranks, NCCL max all-reduce of amax",
+                                      "layout (291 BF16 tensors), rows split over ranks; "
+                                      + ("one launch per step, per-group amax exchanged between ranks inside the "
+                                         "kernel over NVLink peer memory" if args.path == "plan" else
+                                         "amax pass, NCCL max all-reduce, cast pass"),
+                       "path": args.path,
                        "tensors": len(specs), "params": total_params, "src_dtype": "bf16", "dst_dtype": "fp8e4m3",
                        "compat": "reference", "parallelism": f"rowsplit{world}",
                        "l2": "inputs larger than L2 (BF16 shard of 16.06 GB / N per rank)"},
-            "hbm_gbs_job": round(job_gbs, 1), "alg_bytes_per_param": 5,
-            "roofline": roofline, "e2e": e2e, "clocks": clocks, "gpu_launches": 3 * args.steps,
-            "parity": parity, "step_breakdown": breakdown,
+            "hbm_gbs_job": round(job_gbs, 1), "alg_bytes_per_param": 3,
+            "roofline": roofline, "e2e": e2e, "clocks": clocks,
+            "gpu_launches": (1 if plan is not None else 3) * args.steps,
+            "parity": parity, "two_pass": two_pass, "ceilings": ceilings,
         }
         if kernels:
             line["kernels"] = kernels
@@ -817,6 +869,9 @@ def main() -> int:
                     help="comma list of per-config kernel lines to run at N=1 (c1,c2,c3,c4)")
     ap.add_argument("--only-kernels", action="store_true",
                     help="run only the per-config kernel lines (profiling); --steps sets the repetitions")
+    ap.add_argument("--path", choices=["plan", "twopass"], default="twopass",
+                    help="checkpoint step: one launch per step (mf_ckpt_plan_run) or the two-pass mf_ckpt_quant_fp8")
+    ap.add_argument("--group-mb", type=float, default=32.0, help="plan: source MB per tensor group (L2 budget)")
     ap.add_argument("--ckpt-layers", type=int, default=32, help="decoder layers of the checkpoint (profiling only)")
     ap.add_argument("--ckpt-vocab", type=int, default=128256, help="vocabulary rows (profiling only)")
     args = ap.parse_args()

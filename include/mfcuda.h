@@ -99,6 +99,7 @@ typedef void* mf_stream; /* cudaStream_t */
 typedef void* mf_event;  /* cudaEvent_t */
 typedef struct mf_fused_kernel_s* mf_fused_kernel;
 typedef struct mf_comm_s* mf_comm;
+typedef struct mf_ckpt_plan_s* mf_ckpt_plan;
 
 /* ---------------------------------------------------------------------
  * Lifecycle and errors
@@ -365,18 +366,55 @@ int mf_ckpt_quant_fp8_noalloc(const mf_chunk_desc* chunks, int32_t n_chunks, int
                               mf_stream stream);
 
 /* ---------------------------------------------------------------------
+ * The checkpoint quantisation step in one launch.  Replaces the same Go
+ * callers as mf_ckpt_quant_fp8 (the reference itself has no quantiser; the
+ * per-tensor rule is the one of mf_fp8_quantize, the encoder
+ * NewF8E4M3FromFloat32 dtype/fp8.go:77-136 / NewF8E5M2FromFloat32
+ * :190-249).  Same codes, scale_inv and amax as mf_ckpt_quant_fp8 with the
+ * same chunk table, bit for bit.
+ *
+ * A plan is built once per chunk table (like the workspace plan of
+ * ir.PlanWorkspace, ir/planner.go:43-96): the tensors are cut into groups of
+ * consecutive tensors of at most group_bytes of this rank's source (0 = 32 MB;
+ * tensor_numel, the global element count of every tensor, makes every rank cut
+ * the same groups; required when world > 1, NULL = this rank's counts), the chunk table and
+ * group table go to device memory, and a small exchange buffer is allocated.
+ * One run is one cooperative kernel: per group an amax phase, then (one group
+ * later, the group's source still in L2) a cast phase, with the per-group amax
+ * exchanged between the ranks inside the kernel through the ranks' exchange
+ * buffers (CUDA IPC peer memory, plain stores and system-scope flags; every
+ * wait bounded, a wait that runs out leaves MF_DEVICE_TIMEOUT in the sticky
+ * status).  All chunks of a plan share one source dtype (F32, F16 or BF16).
+ *
+ * world > 1: create on every rank, pass each rank's 64-byte ipc_handle to all
+ * ranks (in rank order, world * 64 bytes) to mf_ckpt_plan_connect, and make
+ * sure every rank has connected before any rank runs (a barrier).  Every rank
+ * must run the plan the same number of times.  A plan is not shared between
+ * streams that run at once.  Destroy on every rank after every rank's last
+ * run has finished (a barrier). */
+int mf_ckpt_plan_create(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors,
+                        const int64_t* tensor_numel, int64_t group_bytes, int32_t world, int32_t rank,
+                        int fp8_dtype, int compat, mf_ckpt_plan* plan, void* ipc_handle);
+int mf_ckpt_plan_connect(mf_ckpt_plan plan, const void* ipc_handles);
+/* One step: d_amax[n_tensors] (may be NULL) gets the global amax,
+ * d_scale_inv[n_tensors] (may be NULL) amax / fp8_max, the chunks' dst the
+ * codes.  One kernel launch; no host sync. */
+int mf_ckpt_plan_run(mf_ckpt_plan plan, float* d_amax, float* d_scale_inv, mf_stream stream);
+int mf_ckpt_plan_info(mf_ckpt_plan plan, int32_t* n_groups, int32_t* grid, int64_t* elements);
+int mf_ckpt_plan_destroy(mf_ckpt_plan plan);
+
+/* ---------------------------------------------------------------------
  * Measurement.  No counterpart in the reference (it has no device code).
- * mf_bw_probe moves bytes in a fixed read:write mix with the access forms of
- * the kernels above (16-byte evict-first loads, 16-byte streaming stores)
- * and does no other work; its rate is the DRAM ceiling of that mix, the
+ * mf_bw_probe moves bytes in a fixed read:write mix with the bulk-copy engine
+ * alone (32 KB cp.async.bulk loads into shared memory and stores out of it,
+ * no thread touches the data); its rate is the DRAM ceiling of that mix, the
  * denominator for a kernel with the same mix.  One step reads in_per_step
  * 16-byte vectors (read k of step s at src + 16 * (k * n_steps + s)) and
  * writes out_per_step (same layout in dst).  Mixes: (1,0) read-only,
  * (0,1) write-only, (1,1) copy, (1,4) decode-shaped, (2,1) cast-shaped.
- * A read-only probe needs d_sink (one uint32_t, written only in a case no
- * data produces).  Buffers 16-byte aligned. */
+ * Buffers 16-byte aligned. */
 int mf_bw_probe(const void* src, int in_per_step, void* dst, int out_per_step, int64_t n_steps,
-                uint32_t* d_sink, mf_stream stream);
+                mf_stream stream);
 
 #ifdef __cplusplus
 }

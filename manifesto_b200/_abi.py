@@ -99,7 +99,13 @@ SIGNATURES: dict[str, list] = {
     "mf_ckpt_cast_pass": [ctypes.POINTER(ChunkDesc), _i32, _i32, _vp, _vp, _int, _int, _vp],
     "mf_ckpt_quant_fp8": [ctypes.POINTER(ChunkDesc), _i32, _i32, _vp, _vp, _int, _int, _vp, _vp],
     "mf_ckpt_quant_fp8_noalloc": [ctypes.POINTER(ChunkDesc), _i32, _i32, _vp, _int, _int, _vp, _vp],
-    "mf_bw_probe": [_vp, _int, _vp, _int, _i64, _vp, _vp],
+    "mf_bw_probe": [_vp, _int, _vp, _int, _i64, _vp],
+    "mf_ckpt_plan_create": [ctypes.POINTER(ChunkDesc), _i32, _i32, ctypes.POINTER(_i64), _i64, _i32, _i32, _int, _int,
+                            ctypes.POINTER(_vp), _vp],
+    "mf_ckpt_plan_connect": [_vp, _vp],
+    "mf_ckpt_plan_run": [_vp, _vp, _vp, _vp],
+    "mf_ckpt_plan_info": [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_i64)],
+    "mf_ckpt_plan_destroy": [_vp],
 }
 
 _lib: ctypes.CDLL | None = None

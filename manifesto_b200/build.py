@@ -29,6 +29,7 @@ SOURCES = [
     "int4.cu",
     "axpy.cu",
     "quant.cu",
+    "ckpt.cu",
     "fused.cu",
     "comm.cu",
     "probe.cu",

@@ -124,6 +124,64 @@ def quantise(chunks: ctypes.Array, n_chunks: int, n_tensors: int, d_amax: int, d
          int(compat), comm.handle if comm is not None else None, stream_handle(stream))
 
 
+class QuantPlan:
+    """mf_ckpt_plan_*: the quantisation step of one chunk table in one kernel launch.
+
+    The tensors are cut into groups of consecutive tensors (at most ``group_bytes`` of
+    this rank's source each); one cooperative kernel runs, per group, an amax phase and
+    -- one group later, while the group's source is still in L2 -- the cast phase, with
+    the per-group amax exchanged between ranks inside the kernel through CUDA IPC peer
+    memory.  Same codes, amax and scale_inv as :func:`quantise` with the same table.
+
+    With ``world > 1`` every rank creates its plan, the ranks' ``ipc_handle`` bytes are
+    gathered in rank order and passed to :meth:`connect` on every rank, and all ranks
+    run the plan the same number of times; destroy it on every rank after a barrier
+    that follows every rank's last run.
+    """
+
+    def __init__(self, chunks: ctypes.Array, n_chunks: int, n_tensors: int, tensor_numel: Sequence[int] | None = None,
+                 group_bytes: int = 0, world: int = 1, rank: int = 0, fp8_dtype: DType = DType.FLOAT8_E4M3,
+                 compat: int = 0):
+        h = ctypes.c_void_p()
+        ipc = ctypes.create_string_buffer(64)
+        numel = (ctypes.c_int64 * max(1, n_tensors))(*[int(x) for x in tensor_numel]) if tensor_numel else None
+        call("mf_ckpt_plan_create", chunks, int(n_chunks), int(n_tensors), numel, int(group_bytes), int(world),
+             int(rank), int(fp8_dtype), int(compat), ctypes.byref(h), ipc if world > 1 else None)
+        self.handle = h.value
+        self.world, self.rank, self.n_tensors = int(world), int(rank), int(n_tensors)
+        self.ipc_handle = ipc.raw if world > 1 else b""
+        self._chunks = chunks  # the plan copied the table; kept only so callers' pointers stay referenced
+
+    def connect(self, handles: Sequence[bytes]) -> None:
+        """Open every other rank's exchange buffer (handles: each rank's ipc_handle, rank order)."""
+        if self.world == 1:
+            return
+        if len(handles) != self.world or any(len(h) != 64 for h in handles):
+            raise InvalidArgument(f"QuantPlan.connect: need {self.world} handles of 64 bytes")
+        buf = ctypes.create_string_buffer(b"".join(handles), 64 * self.world)
+        call("mf_ckpt_plan_connect", self.handle, buf)
+
+    def connect_via_store(self, store, key: str = "mfcuda_ckpt_plan") -> None:
+        """Gather the handles through a torch.distributed Store and connect."""
+        if self.world == 1:
+            return
+        store.set(f"{key}/{self.rank}", self.ipc_handle)
+        self.connect([bytes(store.get(f"{key}/{r}")) for r in range(self.world)])
+
+    def run(self, d_amax: int | None, d_scale_inv: int | None, stream=None) -> None:
+        call("mf_ckpt_plan_run", self.handle, d_amax, d_scale_inv, stream_handle(stream))
+
+    def info(self) -> dict:
+        g, grid, n = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int64()
+        call("mf_ckpt_plan_info", self.handle, ctypes.byref(g), ctypes.byref(grid), ctypes.byref(n))
+        return {"groups": g.value, "grid": grid.value, "elements": n.value}
+
+    def close(self) -> None:
+        if self.handle:
+            call("mf_ckpt_plan_destroy", self.handle)
+        self.handle = None
+
+
 class StreamedQuantiser:
     """Quantise checkpoints that live in (pinned) host memory, one after another.
 

@@ -9,9 +9,10 @@
 //               or NewF8E5M2FromFloat32           (dtype/fp8.go:190-249)
 //   scale_inv = amax / fp8_max in float32, 1 if amax is 0 or not finite
 //
-// amax is computed on the integer bit patterns: for every IEEE-like format
-// |v| orders like (bits & ~sign) once NaN codes are excluded, so a BF16
-// pair is folded with one masked __vmaxu2 and the maximum code is decoded
+// amax keeps a running magnitude key per lane: a BF16/F16 pair is folded
+// with one max.xorsign.abs.{bf16,f16}x2 (max of the magnitudes per half, a
+// NaN half never wins), float32 and FP8 on the integer bit patterns (|v|
+// orders like bits & ~sign once NaN codes are excluded); the key is decoded
 // once at the end.  Roofline: HBM; amax reads src once, the cast reads src
 // and writes 1 B per element.
 //
@@ -55,15 +56,16 @@ struct MagKey<MF_DT_F32> {
     }
     static __device__ __forceinline__ float to_f32(uint32_t m) { return __uint_as_float(m); }
 };
+// Two halves per word: max(|a|, |b|) per half with one max.xorsign.abs (the
+// maxNum rule: a NaN half never wins; the result's sign bits are the XOR of the
+// inputs' and are cleared when the key is read).
 template <int DT>
 struct MagKey16 {
-    // two halves per word: (h & 0x7fff) with NaN codes (> nan_floor) zeroed
-    static __device__ __forceinline__ uint32_t fold(const RawChunk<2>& r, uint32_t m, uint32_t nan_floor2) {
+    static __device__ __forceinline__ uint32_t fold(const RawChunk<2>& r, uint32_t m) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            const uint32_t a = r.w[k] & 0x7fff7fffu;
-            const uint32_t nan_mask = __vcmpgtu2(a, nan_floor2);
-            m = __vmaxu2(m, a & ~nan_mask);
+            if constexpr (DT == MF_DT_BF16) asm("max.xorsign.abs.bf16x2 %0, %0, %1;" : "+r"(m) : "r"(r.w[k]));
+            else asm("max.xorsign.abs.f16x2 %0, %0, %1;" : "+r"(m) : "r"(r.w[k]));
         }
         return m;
     }
@@ -71,20 +73,20 @@ struct MagKey16 {
 template <>
 struct MagKey<MF_DT_BF16> {
     static __device__ __forceinline__ uint32_t fold(const RawChunk<2>& r, uint32_t m) {
-        return MagKey16<MF_DT_BF16>::fold(r, m, 0x7f807f80u);
+        return MagKey16<MF_DT_BF16>::fold(r, m);
     }
     static __device__ __forceinline__ float to_f32(uint32_t m) {
-        const uint32_t h = max(m & 0xffffu, m >> 16);
+        const uint32_t h = max(m & 0x7fffu, (m >> 16) & 0x7fffu);
         return __uint_as_float(h << 16);
     }
 };
 template <>
 struct MagKey<MF_DT_F16> {
     static __device__ __forceinline__ uint32_t fold(const RawChunk<2>& r, uint32_t m) {
-        return MagKey16<MF_DT_F16>::fold(r, m, 0x7c007c00u);
+        return MagKey16<MF_DT_F16>::fold(r, m);
     }
     static __device__ __forceinline__ float to_f32(uint32_t m) {
-        const uint32_t h = max(m & 0xffffu, m >> 16);
+        const uint32_t h = max(m & 0x7fffu, (m >> 16) & 0x7fffu);
         return __uint_as_float(f16_to_f32bits(h));
     }
 };

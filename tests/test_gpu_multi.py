@@ -4,11 +4,13 @@ One process per GPU; each quantises its row range of every tensor with
 mf_ckpt_quant_fp8 and the NCCL max all-reduce of the amax vector between the
 two passes.  The shards, put back together, must equal the CPU oracle's
 single-process quantisation bit for bit; mf_ckpt_quant_fp8_noalloc over the
-same communicator must give the same bytes.  NCCL runs with its defaults, as
+same communicator, and the one-launch plan (its amax exchanged inside the
+kernel through the two GPUs' exchange buffers), must give the same bytes.  NCCL runs with its defaults, as
 in bench.py.  Skipped with fewer than 2 GPUs.
 """
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -71,8 +73,30 @@ def _rank_main(rank: int, port: int, out_dir: str) -> None:
     sync_device()
     noalloc_same = all(np.array_equal(fetch(d, n), o) for d, n, o in zip(na_dsts, sizes, out)) and np.array_equal(
         fetch(na_si, 4 * len(specs)), fetch(si, 4 * len(specs)))
+    # the one-launch plan (amax exchanged inside the kernel over peer memory), small groups, three runs
+    pl_dsts = [empty(n) for n in sizes]
+    pl_am, pl_si = empty(4 * len(specs)), empty(4 * len(specs))
+    pl_entries = [(e[0], d.ptr, e[2], e[3], e[4]) for e, d in zip(entries, pl_dsts)]
+    plan = checkpoint.QuantPlan(checkpoint.make_chunks(pl_entries), len(pl_entries), len(specs),
+                                tensor_numel=[s.numel for s in specs], group_bytes=300_000, world=WORLD, rank=rank)
+    assert plan.info()["groups"] > 3
+    plan.connect_via_store(store)
+    plan_same = True
+    for _ in range(3):
+        plan.run(pl_am.ptr, pl_si.ptr)
+        sync_device()
+        plan_same &= all(np.array_equal(fetch(d, n), o) for d, n, o in zip(pl_dsts, sizes, out))
+        plan_same &= np.array_equal(fetch(pl_si, 4 * len(specs)), fetch(si, 4 * len(specs)))
+        plan_same &= np.array_equal(fetch(pl_am, 4 * len(specs)), fetch(am, 4 * len(specs)))
+    # every rank's last run has finished before any exchange buffer is freed
+    store.add("plan_done", 1)
+    deadline = time.time() + 60
+    while int(store.add("plan_done", 0)) < WORLD and time.time() < deadline:
+        time.sleep(0.01)
+    plan.close()
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), amax=fetch(am, 4 * len(specs), np.float32),
-             scale_inv=fetch(si, 4 * len(specs), np.float32), noalloc_same=np.array([noalloc_same]), *out)
+             scale_inv=fetch(si, 4 * len(specs), np.float32), noalloc_same=np.array([noalloc_same]),
+             plan_same=np.array([plan_same]), *out)
     comm.close()
 
 
@@ -97,6 +121,7 @@ def test_two_gpu_nccl_quantisation(backend, ref, tmp_path):
         want_amax = ref.amax(full, ref.BF16)
         for r in range(WORLD):
             assert bool(res[r]["noalloc_same"][0]), r
+            assert bool(res[r]["plan_same"][0]), r
             assert res[r]["amax"][t] == want_amax, (s.name, r)
             assert res[r]["scale_inv"][t] == ref.fp8_scale_inv(want_amax, ref.E4M3)
         got = np.concatenate([res[r][f"arr_{t}"] for r in range(WORLD)])

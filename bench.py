@@ -241,7 +241,7 @@ def probe_ceiling(torch, stream_handle: int, src_ptr: int, a: int, dst_ptr: int,
             "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1), "kernel": f"bw_probe_kernel<{a},{b}>"}
 
 
-KERNEL_CONFIGS = ("c1", "c2", "c3", "c4")
+KERNEL_CONFIGS = ("c1", "c2", "c3", "c4", "c4g")
 
 
 def bench_kernels(torch, stream_handle: int, peak: float, which=KERNEL_CONFIGS, reps: int = 50) -> dict:
@@ -257,7 +257,7 @@ def bench_kernels(torch, stream_handle: int, peak: float, which=KERNEL_CONFIGS, 
         torch.amax(flush_words)
     out = {}
     for name in which:
-        out.update({"c1": _kernel_c1, "c2": _kernel_c2, "c3": _kernel_c3, "c4": _kernel_c4}[name](
+        out.update({"c1": _kernel_c1, "c2": _kernel_c2, "c3": _kernel_c3, "c4": _kernel_c4, "c4g": _kernel_c4g}[name](
             torch, stream_handle, peak, flush, reps))
         torch.cuda.empty_cache()
     del flush_buf
@@ -367,6 +367,32 @@ def _kernel_c4(torch, stream_handle, peak, flush, reps) -> dict:
     out["c4_fused_swiglu_fp8"]["single_pass_lower_bound_bytes"] = 5 * n
     k.close()
     return out
+
+
+def _kernel_c4g(torch, stream_handle, peak, flush, reps) -> dict:
+    """A chain with no specialised kernel, on config 4's shape: Gelu(Add(Mul(x, gamma), beta)) on BF16
+    [64, 2048, 4096], gamma/beta broadcast over the last dimension, BF16 out (the generic fused path)."""
+    from manifesto_b200 import fusion
+    from manifesto_b200.dtype import DType
+    hidden = 4096
+    n = 64 * 2048 * hidden
+    x = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    fill_normal_bf16(torch, x, 43, 0.0, 1.0)
+    g = (torch.randn(hidden, device="cuda") * 0.1 + 1.0).to(torch.bfloat16)
+    be = (torch.randn(hidden, device="cuda") * 0.1).to(torch.bfloat16)
+    o = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    k = fusion.emit_cuda(fusion.gelu_affine_chain(), in_dtypes=[DType.BFLOAT16] * 3, in_bcast=[0, hidden, hidden],
+                         out_dtype=DType.BFLOAT16)
+    assert not k.specialised()
+    ptrs = [x.data_ptr(), g.data_ptr(), be.data_ptr()]
+    f = lambda: k.run(ptrs, o.data_ptr(), n, stream=stream_handle)
+    _warm(f)
+    times = time_launches(torch, f, reps, flush)
+    # read x, write out: the copy-shaped 1:1 mix
+    ceiling = probe_ceiling(torch, stream_handle, x.data_ptr(), 1, o.data_ptr(), 1, n * 2 // 16, flush)
+    line = kernel_line("fused_interp_kernel<BF16> (Gelu(Add(Mul(x,g),b)))", 4 * n, times, peak, n, ceiling)
+    k.close()
+    return {"c4g_fused_gelu_generic": line}
 
 
 def run_ours(args, world: int, rank: int, local_rank: int) -> None:
@@ -820,6 +846,14 @@ def cpu_kernel_baselines(which=KERNEL_CONFIGS) -> dict:
         leg("c4_fused_swiglu_fp8", n, c4,
             "evalCPU of Mul(Silu(Add(Mul(x,g),b)),y) to BF16, amax, scaled E4M3 cast over 2^22 elements "
             "(1/128 of config 4)")
+    if "c4g" in which:
+        hidden, n = 4096, 1 << 22
+        ins = [synthetic.normal_bf16(0x5EED0014, n), synthetic.normal_bf16(0x5EED1014, hidden, 1.0, 0.1),
+               synthetic.normal_bf16(0x5EED2014, hidden, 0.0, 0.1)]
+        tree = fusion.node_table(fusion.gelu_affine_chain().root)
+        leg("c4g_fused_gelu_generic", n,
+            lambda th: ref.fused_eval(tree, ins, [ref.BF16] * 3, [0, hidden, hidden], ref.BF16, n, threads=th),
+            "evalCPU of Gelu(Add(Mul(x,g),b)) to BF16 over 2^22 elements (1/128 of config 4's shape)")
     return out
 
 
@@ -866,7 +900,7 @@ def main() -> int:
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-config kernel lines (N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernels", default=",".join(KERNEL_CONFIGS),
-                    help="comma list of per-config kernel lines to run at N=1 (c1,c2,c3,c4)")
+                    help="comma list of per-config kernel lines to run at N=1 (c1,c2,c3,c4,c4g)")
     ap.add_argument("--only-kernels", action="store_true",
                     help="run only the per-config kernel lines (profiling); --steps sets the repetitions")
     ap.add_argument("--path", choices=["plan", "twopass"], default="twopass",

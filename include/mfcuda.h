@@ -259,12 +259,18 @@ typedef struct mf_fused_program {
     int32_t out_dtype;        /* F32, F16 or BF16 */
 } mf_fused_program;
 
-/* Validate and upload a program; picks a hand-specialised kernel when the
- * program matches one (e.g. Mul(Silu(Add(Mul(x,g),b)),y)), else the
- * generic interpreter.  Host-synchronous (one small upload). */
+/* Validate a program; picks a hand-specialised kernel when the program
+ * matches one (e.g. Mul(Silu(Add(Mul(x,g),b)),y)), and emits CUDA source for
+ * the expression and compiles it with NVRTC for sm_100a (the CUDA
+ * counterpart of the Metal target's shader emission, codegen/metal.go:79-227;
+ * 0.1-0.5 s, once per distinct program in a process).  Without NVRTC the
+ * runtime interpreter runs the program.  Needs no device. */
 int mf_fused_compile(const mf_fused_program* program, mf_fused_kernel* kernel);
 int mf_fused_destroy(mf_fused_kernel kernel);
-/* 1 if the compiled kernel runs a hand-specialised body, else 0. */
+/* Which device code runs the kernel: 1 a hand-specialised body (the SwiGLU
+ * chain), 2 CUDA source generated for this expression and compiled with NVRTC
+ * for sm_100a at mf_fused_compile, 0 the runtime interpreter (used when NVRTC
+ * is unavailable or MF_FUSED_JIT=0; mf_last_error then gives the reason). */
 int mf_fused_is_specialised(mf_fused_kernel kernel, int* specialised);
 /* out: n elements of out_dtype.  If d_amax is not NULL, the kernel also
  * folds max|out| (of the encoded values, NaN ignored) into *d_amax with an

@@ -14,9 +14,10 @@
 // (read once, write FP8 once).  A tensor too large for the L2 budget is cast
 // from DRAM again, as in the two-pass form.
 //
-// Tiles are dealt round-robin over one numbering that runs through all groups,
-// so every CTA gets the same share of every group to within one tile and the
-// extra tile moves from CTA to CTA.
+// Every CTA gets a contiguous range of each group's tiles; the CTAs that take
+// the group's one extra tile start after the group's first tile number, so the
+// extra tile moves from CTA to CTA from group to group (MF_PLAN_DEAL=1 deals
+// tiles round-robin instead, measured slower).
 //
 // The cast tiles of a group need its amax over every CTA and every rank.  When
 // a CTA has folded its amax tiles of group g its consumer warps meet at a named
@@ -64,9 +65,10 @@ namespace {
 //   MF_PLAN_CAST_HINT   L2 policy of the cast phase's loads
 //   MF_PLAN_REVERSE     1: the cast phase walks each CTA's tiles last to first (the tiles the amax
 //                       phase read last are the likeliest still in L2)
+//   MF_PLAN_DEAL        1: tiles dealt round-robin across CTAs; 0: contiguous ranges
 //   MF_PLAN_GROUP_MB    default group budget
 #ifndef MF_PLAN_LEAD
-#define MF_PLAN_LEAD 2
+#define MF_PLAN_LEAD 8
 #endif
 #ifndef MF_PLAN_STAGE_KB
 #define MF_PLAN_STAGE_KB 64
@@ -82,6 +84,9 @@ namespace {
 #endif
 #ifndef MF_PLAN_REVERSE
 #define MF_PLAN_REVERSE 0
+#endif
+#ifndef MF_PLAN_DEAL
+#define MF_PLAN_DEAL 0
 #endif
 #ifndef MF_PLAN_GROUP_MB
 #define MF_PLAN_GROUP_MB 32
@@ -235,16 +240,25 @@ struct PlanGeometry {
 // within a group CTAs differ by at most one tile, and the CTA that gets the
 // extra one moves on from group to group, so no CTA falls behind over a run.
 struct CtaTiles {
-    int64_t first, count;
+    int64_t first, count, step;
     __device__ __forceinline__ int64_t tile(int64_t j, bool reverse) const {
-        return first + (reverse ? count - 1 - j : j) * static_cast<int64_t>(gridDim.x);
+        return first + (reverse ? count - 1 - j : j) * step;
     }
 };
 __device__ __forceinline__ CtaTiles cta_tiles(const PlanGroup& grp) {
     const int64_t n = gridDim.x;
+#if MF_PLAN_DEAL
     int64_t f = (static_cast<int64_t>(blockIdx.x) - grp.base) % n;
     if (f < 0) f += n;
-    return {f, grp.tiles > f ? (grp.tiles - 1 - f) / n + 1 : 0};
+    return {f, grp.tiles > f ? (grp.tiles - 1 - f) / n + 1 : 0, n};
+#else
+    // contiguous ranges, the extra tiles going to the CTAs after this group's base
+    const int64_t per = grp.tiles / n, extra = grp.tiles % n;
+    int64_t b = (static_cast<int64_t>(blockIdx.x) - grp.base) % n;
+    if (b < 0) b += n;
+    const int64_t lo = b * per + (b < extra ? b : extra);
+    return {lo, per + (b < extra ? 1 : 0), 1};
+#endif
 }
 
 // The chunk of [c0, c1) that holds group tile t.
@@ -257,6 +271,23 @@ __device__ __forceinline__ int group_chunk(const ChunkRec* ch, int c0, int c1, i
     }
     return lo;
 }
+
+// The chunk of the tile last asked for, with its tile range [lo, hi) in the
+// group: a CTA's tiles of a group come in order, so the chunk table is searched
+// only when a tile leaves the current chunk.
+struct ChunkCursor {
+    int k = 0;
+    int64_t lo = 0, hi = -1;
+    __device__ __forceinline__ void reset() { lo = 0; hi = -1; }
+    __device__ __forceinline__ const ChunkRec& at(const ChunkRec* ch, const PlanGroup& g, int64_t t) {
+        if (t < lo || t >= hi) {
+            k = group_chunk(ch, g.c0, g.c1, t);
+            lo = ch[k].tile_begin;
+            hi = (k + 1 < g.c1) ? ch[k + 1].tile_begin : g.tiles;
+        }
+        return ch[k];
+    }
+};
 
 // The 256 consumer threads of the CTA (named barrier 1; the producer warp never joins).
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kStreamThreads) : "memory"); }
@@ -374,9 +405,12 @@ __global__ void __launch_bounds__(kStreamBlock, kPlanCtas) ckpt_plan_kernel(cons
         const uint64_t keep = l2_policy_evict_last(), drop = l2_policy_evict_first();
         int64_t i = 0;
         bool ok = true;
+        ChunkCursor cur_a, cur_c;
         for (int k = 0; k <= n_groups && ok; ++k) {
+            cur_a.reset();
+            cur_c.reset();
             PlanGroup ga{}, gc{};
-            CtaTiles ta{0, 0}, tc{0, 0};
+            CtaTiles ta{0, 0, 1}, tc{0, 0, 1};
             if (k < n_groups) {
                 ga = a.groups[k];
                 ta = cta_tiles(ga);
@@ -396,7 +430,7 @@ __global__ void __launch_bounds__(kStreamBlock, kPlanCtas) ckpt_plan_kernel(cons
                     break;
                 }
                 ++i;
-                const ChunkRec& ch = a.chunks[group_chunk(a.chunks, grp.c0, grp.c1, t)];
+                const ChunkRec& ch = am ? cur_a.at(a.chunks, grp, t) : cur_c.at(a.chunks, grp, t);
                 const int64_t e0 = (t - ch.tile_begin) * G::kTileElems;
                 const int64_t cnt = min(G::kTileElems, ch.n - e0);
                 const uint32_t bytes = static_cast<uint32_t>((cnt * kIn) & ~int64_t(15));
@@ -482,7 +516,7 @@ __global__ void __launch_bounds__(kStreamBlock, kPlanCtas) ckpt_plan_kernel(cons
 
     for (int k = 0; k <= n_groups; ++k) {
         PlanGroup ga{}, gc{};
-        CtaTiles ta{0, 0}, tc{0, 0};
+        CtaTiles ta{0, 0, 1}, tc{0, 0, 1};
         if (k < n_groups) {
             ga = a.groups[k];
             ta = cta_tiles(ga);
@@ -493,6 +527,7 @@ __global__ void __launch_bounds__(kStreamBlock, kPlanCtas) ckpt_plan_kernel(cons
         }
         const bool writer = k >= 1 && static_cast<int>(blockIdx.x) == (k - 1) % static_cast<int>(gridDim.x);
         Segment sg{ta.count, tc.count};
+        ChunkCursor ccur_a, ccur_c;
         uint32_t key = 0;
         float mel = 0.0f;
         int cur_a = -1, cur_c = -1;
@@ -514,7 +549,7 @@ __global__ void __launch_bounds__(kStreamBlock, kPlanCtas) ckpt_plan_kernel(cons
                 dead = true;
             }
             if (!dead) {
-                const ChunkRec& ch = a.chunks[group_chunk(a.chunks, grp.c0, grp.c1, t)];
+                const ChunkRec& ch = am ? ccur_a.at(a.chunks, grp, t) : ccur_c.at(a.chunks, grp, t);
                 const int64_t e0 = (t - ch.tile_begin) * G::kTileElems;
                 const int64_t cnt = min(G::kTileElems, ch.n - e0);
                 if (am) {

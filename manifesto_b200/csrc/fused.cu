@@ -23,17 +23,12 @@
 #include <algorithm>
 #include <cstring>
 #include <new>
+#include <string>
 
+#include "mf_fused_ops.cuh"
 #include "mf_internal.h"
 #include "mf_runtime.h"
 #include "mf_vec.cuh"
-
-// optimizer.NodeType values, optimizer/fusion_ast.go:32-65
-enum NodeType : int32_t {
-    NODE_INVALID = 0, NODE_INPUT, NODE_CONSTANT, NODE_ADD, NODE_SUB, NODE_MUL, NODE_DIV, NODE_MAX, NODE_MIN,
-    NODE_NEG, NODE_ABS, NODE_SQRT, NODE_EXP, NODE_LOG, NODE_RELU, NODE_SIGMOID, NODE_TANH, NODE_SILU,
-    NODE_GELU, NODE_LEAKY_RELU
-};
 
 struct mf_fused_kernel_s;
 
@@ -79,47 +74,6 @@ __device__ __forceinline__ float load_input(int dt, const void* p, int64_t i) {
     }
 }
 
-// sqrt(2/pi) in float64: Go folds the constant 2/math.Pi exactly and math.Sqrt
-// rounds once (codegen/cpu.go:198).
-__device__ __forceinline__ double gelu_k() { return sqrt(0.63661977236758134307553505349005744813783858296182579499); }
-
-__device__ __forceinline__ float apply_unary(int op, float v) {
-    switch (op) {
-    case NODE_NEG: return -v;
-    case NODE_ABS: return v < 0.0f ? -v : v;
-    case NODE_SQRT: return f64_to_f32(sqrt(static_cast<double>(v)));
-    case NODE_EXP: return f64_to_f32(exp(static_cast<double>(v)));
-    case NODE_LOG: return f64_to_f32(log(static_cast<double>(v)));
-    case NODE_RELU: return v < 0.0f ? 0.0f : v;
-    case NODE_SIGMOID: return f64_to_f32(__drcp_rn(__dadd_rn(1.0, exp(-static_cast<double>(v)))));
-    case NODE_TANH: return f64_to_f32(tanh(static_cast<double>(v)));
-    case NODE_SILU: {
-        const double d = static_cast<double>(v);
-        return f64_to_f32(__ddiv_rn(d, __dadd_rn(1.0, exp(-d))));
-    }
-    case NODE_GELU: {
-        const double d = static_cast<double>(v);
-        const double cube = __dmul_rn(__dmul_rn(__dmul_rn(0.044715, d), d), d);
-        const double inner = __dmul_rn(gelu_k(), __dadd_rn(d, cube));
-        return f64_to_f32(__dmul_rn(__dmul_rn(0.5, d), __dadd_rn(1.0, tanh(inner))));
-    }
-    case NODE_LEAKY_RELU: return v >= 0.0f ? v : __fmul_rn(0.01f, v);
-    default: return 0.0f;
-    }
-}
-
-__device__ __forceinline__ float apply_binary(int op, float a, float b) {
-    switch (op) {
-    case NODE_ADD: return __fadd_rn(a, b);
-    case NODE_SUB: return __fsub_rn(a, b);
-    case NODE_MUL: return __fmul_rn(a, b);
-    case NODE_DIV: return __fdiv_rn(a, b);
-    case NODE_MAX: return a > b ? a : b;
-    case NODE_MIN: return a < b ? a : b;
-    default: return 0.0f;
-    }
-}
-
 __device__ __forceinline__ int64_t bcast_index(int64_t i, int64_t l) {
     if (l <= 0) return i;
     if (i < (int64_t(1) << 32) && l < (int64_t(1) << 32))
@@ -139,9 +93,9 @@ __device__ __forceinline__ float eval_program(const FusedProgram& p, const Input
             st[sp++] = __uint_as_float(p.const_bits[p.arg[k]]);
         } else if (op >= NODE_ADD && op <= NODE_MIN) {
             const float b = st[--sp];
-            st[sp - 1] = apply_binary(op, st[sp - 1], b);
+            st[sp - 1] = fused_binary_rt(op, st[sp - 1], b);
         } else {
-            st[sp - 1] = apply_unary(op, st[sp - 1]);
+            st[sp - 1] = fused_unary_rt(op, st[sp - 1]);
         }
     }
     return st[0];
@@ -157,14 +111,7 @@ __global__ void __launch_bounds__(kThreads) fused_interp_kernel(const __grid_con
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
         const uint32_t code = encode_f32<ODT>(eval_program(p, in, i), 0);
         store_code<ODT>(out, i, code);
-        if (d_amax) {
-            // |stored value|, NaN ignored
-            float a;
-            if constexpr (ODT == MF_DT_F32) a = fabsf(__uint_as_float(code));
-            else if constexpr (ODT == MF_DT_BF16) a = fabsf(__uint_as_float(code << 16));
-            else a = fabsf(__uint_as_float(f16_to_f32bits(code)));
-            m = (a > m) ? a : m;
-        }
+        if (d_amax) m = fmaxf(m, stored_abs<ODT>(code));  // |stored value|, NaN ignored
     }
     if (d_amax) {
         // block reduce
@@ -209,7 +156,7 @@ __device__ __forceinline__ float rcp_ftz(float x) {
 }
 
 // The interpreter's float64 SiLU, out of line: the hot loop keeps its registers.
-static __device__ __noinline__ float silu_f64(float t) { return apply_unary(NODE_SILU, t); }
+static __device__ __noinline__ float silu_f64(float t) { return fused_unary<NODE_SILU>(t); }
 
 // Running max(|acc|, |w|) per BF16 half (maxNum: a NaN half never wins).  The
 // result's sign bits are the XOR of the inputs' signs and mean nothing; the
@@ -365,7 +312,11 @@ int64_t swiglu_rows_grid(int64_t row_vecs, int64_t target) {
 
 struct mf_fused_kernel_s {
     mf::FusedProgram prog;
+    int n_consts = 0;
     int max_depth = 0;
+    // the generated kernel of the CUDA codegen target (NULL: the interpreter runs the program)
+    mf::JitKernel* jit = nullptr;
+    std::string jit_why;
     // specialisation: 0 = interpreter, 1 = SwiGLU-style BF16 chain
     int special = 0;
     int sx = -1, sg = -1, sb = -1, sy = -1;  // input slots of x, g, b, y
@@ -488,6 +439,8 @@ int launch_fused(const mf_fused_kernel_s& k, const void* const* inputs, void* ou
             else
                 swiglu_bf16_kernel<false><<<grid, kThreads, 0, s>>>(x, y, g, b, o, nvec, row_vecs, nullptr);
         }
+    } else if (k.jit) {
+        return jit_launch(k.jit, inputs, out, n, d_amax, s);
     } else {
         switch (k.prog.out_dtype) {
         case MF_DT_BF16: launch_interp<MF_DT_BF16>(k, in, out, n, d_amax, s); break;
@@ -570,19 +523,27 @@ extern "C" int mf_fused_compile(const mf_fused_program* program, mf_fused_kernel
         return fail(MF_ERR_INVALID_ARGUMENT, "codegen cuda: expression needs %d stack slots (max %d)", max_depth, kMaxStack);
     }
     k->max_depth = max_depth;
+    k->n_consts = p.n_consts;
     detect_swiglu(*k);
+    // the CUDA codegen target: source for this expression, compiled for sm_100a (the
+    // interpreter stays in charge when NVRTC is unavailable)
+    const JitSpec spec{k->prog.n_nodes, k->prog.op,       k->prog.arg,      p.n_consts,       k->prog.const_bits,
+                       k->prog.n_inputs, k->prog.in_dtype, k->prog.in_bcast, k->prog.out_dtype};
+    k->jit = jit_compile(spec, &k->jit_why);
     *kernel = k;
     return MF_OK;
 }
 
 extern "C" int mf_fused_destroy(mf_fused_kernel kernel) {
+    if (kernel) jit_release(kernel->jit);
     delete kernel;
     return MF_OK;
 }
 
 extern "C" int mf_fused_is_specialised(mf_fused_kernel kernel, int* specialised) {
     if (!kernel || !specialised) return fail(MF_ERR_INVALID_ARGUMENT, "mf_fused_is_specialised: NULL argument");
-    *specialised = kernel->special;
+    *specialised = kernel->special ? 1 : kernel->jit ? 2 : 0;
+    if (!kernel->special && !kernel->jit) fail(MF_OK, "interpreter: %s", kernel->jit_why.c_str());
     return MF_OK;
 }
 

@@ -1,0 +1,103 @@
+// mf_fused_ops.cuh -- element semantics of a fused elementwise chain.
+//
+// One place for the per-node rules of manifesto's evalCPU
+// (codegen/cpu.go:126-212), shared by the runtime interpreter (fused.cu) and
+// by the CUDA source the CUDA codegen target emits for each FusionAST and
+// compiles at run time (fused_jit.cu), so the two cannot drift apart:
+//   Add/Sub/Mul/Div/Max/Min/Neg/Abs/ReLU/LeakyReLU in float32, nothing
+//   contracted (Max: l > r ? l : r, :144-151; Min :153-160; Abs :165-170;
+//   ReLU v < 0 ? 0 : v, :178-184; LeakyReLU slope 0.01, :201-206);
+//   Sqrt/Exp/Log/Sigmoid/Tanh/SiLU/GELU in float64, then float32(...) with
+//   the amd64 NaN rule (:172-200); GELU's sqrt(2/pi) folded in float64 (:198).
+// Unknown nodes evaluate to 0 (:208-210).
+#pragma once
+
+#include "mf_numerics.cuh"
+
+// optimizer.NodeType values, optimizer/fusion_ast.go:32-65
+enum NodeType : int32_t {
+    NODE_INVALID = 0, NODE_INPUT, NODE_CONSTANT, NODE_ADD, NODE_SUB, NODE_MUL, NODE_DIV, NODE_MAX, NODE_MIN,
+    NODE_NEG, NODE_ABS, NODE_SQRT, NODE_EXP, NODE_LOG, NODE_RELU, NODE_SIGMOID, NODE_TANH, NODE_SILU,
+    NODE_GELU, NODE_LEAKY_RELU
+};
+
+namespace mf {
+
+// sqrt(2/pi) in float64: Go folds the constant 2/math.Pi exactly and math.Sqrt
+// rounds once (codegen/cpu.go:198).
+__device__ __forceinline__ double gelu_k() { return sqrt(0.63661977236758134307553505349005744813783858296182579499); }
+
+template <int OP>
+__device__ __forceinline__ float fused_unary(float v) {
+    if constexpr (OP == NODE_NEG) return -v;
+    else if constexpr (OP == NODE_ABS) return v < 0.0f ? -v : v;
+    else if constexpr (OP == NODE_SQRT) return f64_to_f32(sqrt(static_cast<double>(v)));
+    else if constexpr (OP == NODE_EXP) return f64_to_f32(exp(static_cast<double>(v)));
+    else if constexpr (OP == NODE_LOG) return f64_to_f32(log(static_cast<double>(v)));
+    else if constexpr (OP == NODE_RELU) return v < 0.0f ? 0.0f : v;
+    else if constexpr (OP == NODE_SIGMOID) return f64_to_f32(__drcp_rn(__dadd_rn(1.0, exp(-static_cast<double>(v)))));
+    else if constexpr (OP == NODE_TANH) return f64_to_f32(tanh(static_cast<double>(v)));
+    else if constexpr (OP == NODE_SILU) {
+        const double d = static_cast<double>(v);
+        return f64_to_f32(__ddiv_rn(d, __dadd_rn(1.0, exp(-d))));
+    } else if constexpr (OP == NODE_GELU) {
+        const double d = static_cast<double>(v);
+        const double cube = __dmul_rn(__dmul_rn(__dmul_rn(0.044715, d), d), d);
+        const double inner = __dmul_rn(gelu_k(), __dadd_rn(d, cube));
+        return f64_to_f32(__dmul_rn(__dmul_rn(0.5, d), __dadd_rn(1.0, tanh(inner))));
+    } else if constexpr (OP == NODE_LEAKY_RELU) return v >= 0.0f ? v : __fmul_rn(0.01f, v);
+    else return 0.0f;
+}
+
+template <int OP>
+__device__ __forceinline__ float fused_binary(float a, float b) {
+    if constexpr (OP == NODE_ADD) return __fadd_rn(a, b);
+    else if constexpr (OP == NODE_SUB) return __fsub_rn(a, b);
+    else if constexpr (OP == NODE_MUL) return __fmul_rn(a, b);
+    else if constexpr (OP == NODE_DIV) return __fdiv_rn(a, b);
+    else if constexpr (OP == NODE_MAX) return a > b ? a : b;
+    else if constexpr (OP == NODE_MIN) return a < b ? a : b;
+    else return 0.0f;
+}
+
+// The same with the node type known only at run time (the interpreter).
+__device__ __forceinline__ float fused_unary_rt(int op, float v) {
+    switch (op) {
+    case NODE_NEG: return fused_unary<NODE_NEG>(v);
+    case NODE_ABS: return fused_unary<NODE_ABS>(v);
+    case NODE_SQRT: return fused_unary<NODE_SQRT>(v);
+    case NODE_EXP: return fused_unary<NODE_EXP>(v);
+    case NODE_LOG: return fused_unary<NODE_LOG>(v);
+    case NODE_RELU: return fused_unary<NODE_RELU>(v);
+    case NODE_SIGMOID: return fused_unary<NODE_SIGMOID>(v);
+    case NODE_TANH: return fused_unary<NODE_TANH>(v);
+    case NODE_SILU: return fused_unary<NODE_SILU>(v);
+    case NODE_GELU: return fused_unary<NODE_GELU>(v);
+    case NODE_LEAKY_RELU: return fused_unary<NODE_LEAKY_RELU>(v);
+    default: return 0.0f;
+    }
+}
+__device__ __forceinline__ float fused_binary_rt(int op, float a, float b) {
+    switch (op) {
+    case NODE_ADD: return fused_binary<NODE_ADD>(a, b);
+    case NODE_SUB: return fused_binary<NODE_SUB>(a, b);
+    case NODE_MUL: return fused_binary<NODE_MUL>(a, b);
+    case NODE_DIV: return fused_binary<NODE_DIV>(a, b);
+    case NODE_MAX: return fused_binary<NODE_MAX>(a, b);
+    case NODE_MIN: return fused_binary<NODE_MIN>(a, b);
+    default: return 0.0f;
+    }
+}
+
+// |stored value| of an output code, NaN ignored (0): the amax fold of a chain
+// whose output is then cast to FP8.
+template <int ODT>
+__device__ __forceinline__ float stored_abs(uint32_t code) {
+    float a;
+    if constexpr (ODT == MF_DT_F32) a = fabsf(__uint_as_float(code));
+    else if constexpr (ODT == MF_DT_BF16) a = fabsf(__uint_as_float(code << 16));
+    else a = fabsf(__uint_as_float(f16_to_f32bits(code)));
+    return (a == a) ? a : 0.0f;
+}
+
+}  // namespace mf

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <string>
 
 #include "../../include/mfcuda.h"
 
@@ -17,5 +18,25 @@ int launch_scaled_cast(const void* src, int src_dtype, void* dst, int fp8_dtype,
 int launch_amax(const void* src, int src_dtype, int64_t n, float* d_amax, cudaStream_t s);
 // In-place float32 max all-reduce over the communicator (comm.cu).
 int comm_allreduce_max(mf_comm comm, float* d_vec, int64_t count, cudaStream_t s);
+
+// A validated fused program (postfix) as the CUDA codegen target sees it (fused_jit.cu).
+struct JitSpec {
+    int n_nodes;
+    const int8_t* op;
+    const int8_t* arg;
+    int n_consts;
+    const uint32_t* const_bits;  // float32(node value) bit patterns
+    int n_inputs;
+    const int32_t* in_dtype;
+    const int64_t* in_bcast;     // 0: full size; L: read at index i mod L
+    int out_dtype;
+};
+struct JitKernel;
+// Emit CUDA source for the program and compile it with NVRTC; NULL (and the
+// reason in *why) when NVRTC is unavailable or the compile fails.
+JitKernel* jit_compile(const JitSpec& spec, std::string* why);
+void jit_release(JitKernel* k);
+// Launch the generated kernel (8 elements per lane when every buffer allows it).
+int jit_launch(JitKernel* k, const void* const* inputs, void* out, int64_t n, float* d_amax, cudaStream_t s);
 
 }  // namespace mf

@@ -201,10 +201,19 @@ class CUDAKernel:
     def output(self) -> str:
         return self.fusion.output_port
 
-    def specialised(self) -> bool:
+    def kind(self) -> int:
+        """1: the hand-written SwiGLU kernel; 2: the kernel generated for this expression; 0: the interpreter."""
         s = ctypes.c_int()
         call("mf_fused_is_specialised", self.handle, ctypes.byref(s))
-        return bool(s.value)
+        return s.value
+
+    def specialised(self) -> bool:
+        """True when the hand-written SwiGLU-chain kernel runs this fusion."""
+        return self.kind() == 1
+
+    def generated(self) -> bool:
+        """True when the CUDA codegen target compiled a kernel for this expression."""
+        return self.kind() == 2
 
     def run(self, inputs: Sequence[int], output: int, count: int, amax: int | None = None, stream=None) -> None:
         """Evaluate the fusion over `count` elements of device buffers."""
@@ -255,3 +264,11 @@ def swiglu_chain() -> FusionAST:
     x, g, b, y = (input_node(i, DType.BFLOAT16) for i in range(4))
     root = binary(NodeType.MUL, unary(NodeType.SILU, binary(NodeType.ADD, binary(NodeType.MUL, x, g), b)), y)
     return FusionAST(root=root, input_ports=["x", "gamma", "beta", "y"], output_port="out", dtype=DType.BFLOAT16)
+
+
+def gelu_affine_chain() -> FusionAST:
+    """Gelu(Add(Mul(x, gamma), beta)): an affine-then-GELU chain (no specialised kernel; the
+    generic CUDA path runs it)."""
+    x, g, b = (input_node(i, DType.BFLOAT16) for i in range(3))
+    root = unary(NodeType.GELU, binary(NodeType.ADD, binary(NodeType.MUL, x, g), b))
+    return FusionAST(root=root, input_ports=["x", "gamma", "beta"], output_port="out", dtype=DType.BFLOAT16)

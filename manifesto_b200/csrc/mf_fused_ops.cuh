@@ -60,6 +60,120 @@ __device__ __forceinline__ float fused_binary(float a, float b) {
     else return 0.0f;
 }
 
+// ------------------------------------------- float32 forms for 16-bit outputs
+//
+// A chain whose output is BF16 or F16 is held to 1 ulp of that format after the
+// final cast (2^-8 or 2^-11 relative), far coarser than float32.  For a node whose
+// value reaches such an output only through operations that keep relative error
+// (Mul, Div, Neg, Abs, ReLU, LeakyReLU, Max, Min -- the code generator checks the
+// path), the generated code evaluates the float64 rule in float32 on the SFU,
+// inside ranges where both this form and the reference's float64 value are
+// accurate to better than 2^-16 relative.  Outside them (NaN, overflow edges,
+// GELU far below zero, where the reference's 1 + tanh(u) in float64 keeps only a
+// few significant bits) the float64 rule runs.  ex2/rcp flush subnormals; inside
+// the ranges their arguments and results are normal.
+__device__ __forceinline__ float sfu_ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float sfu_rcp(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <int OP>
+__device__ __forceinline__ float fused_unary_fast(float v) {
+    constexpr float kLog2e = 1.4426950408889634f;
+    if constexpr (OP == NODE_EXP) {
+        if (v >= -80.0f && v <= 88.0f) return sfu_ex2(__fmul_rn(v, kLog2e));
+    } else if constexpr (OP == NODE_SIGMOID) {
+        if (v >= -80.0f) return sfu_rcp(__fadd_rn(1.0f, sfu_ex2(__fmul_rn(v, -kLog2e))));
+    } else if constexpr (OP == NODE_SILU) {
+        if (v >= -80.0f) return __fmul_rn(v, sfu_rcp(__fadd_rn(1.0f, sfu_ex2(__fmul_rn(v, -kLog2e)))));
+    } else if constexpr (OP == NODE_TANH) {
+        if (v == v) return tanhf(v);
+    } else if constexpr (OP == NODE_LOG) {
+        if (v >= 1.0e-30f && v <= 1.0e30f) return logf(v);
+    } else if constexpr (OP == NODE_SQRT) {
+        if (v >= 0.0f) return __fsqrt_rn(v);
+    } else if constexpr (OP == NODE_GELU) {
+        // 0.5 x (1 + tanh(u)) = x / (1 + e^(-2u)), u = sqrt(2/pi) (x + 0.044715 x^3)
+        const float u =
+            __fmul_rn(0.7978845608028654f, __fadd_rn(v, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, v), v), v)));
+        if (u >= -9.0f && v <= 3.0e38f)
+            return __fmul_rn(v, sfu_rcp(__fadd_rn(1.0f, sfu_ex2(__fmul_rn(u, -2.0f * kLog2e)))));
+    }
+    return fused_unary<OP>(v);
+}
+
+// fused_unary_fast without the branch: always the float32 form, and `bad` set
+// when the input lies outside its range.  The caller re-evaluates an element
+// that set it with fused_unary_fast (one branch per group of elements instead
+// of one per element).
+template <int OP>
+__device__ __forceinline__ float fused_unary_try(float v, bool& bad) {
+    constexpr float kLog2e = 1.4426950408889634f;
+    if constexpr (OP == NODE_EXP) {
+        bad |= !(v >= -80.0f && v <= 88.0f);
+        return sfu_ex2(__fmul_rn(v, kLog2e));
+    } else if constexpr (OP == NODE_SIGMOID) {
+        bad |= !(v >= -80.0f);
+        return sfu_rcp(__fadd_rn(1.0f, sfu_ex2(__fmul_rn(v, -kLog2e))));
+    } else if constexpr (OP == NODE_SILU) {
+        bad |= !(v >= -80.0f);
+        return __fmul_rn(v, sfu_rcp(__fadd_rn(1.0f, sfu_ex2(__fmul_rn(v, -kLog2e)))));
+    } else if constexpr (OP == NODE_TANH) {
+        bad |= (v != v);
+        return tanhf(v);
+    } else if constexpr (OP == NODE_LOG) {
+        bad |= !(v >= 1.0e-30f && v <= 1.0e30f);
+        return logf(v);
+    } else if constexpr (OP == NODE_SQRT) {
+        bad |= !(v >= 0.0f);
+        return __fsqrt_rn(v);
+    } else if constexpr (OP == NODE_GELU) {
+        const float u =
+            __fmul_rn(0.7978845608028654f, __fadd_rn(v, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, v), v), v)));
+        bad |= !(u >= -9.0f && v <= 3.0e38f);
+        return __fmul_rn(v, sfu_rcp(__fadd_rn(1.0f, sfu_ex2(__fmul_rn(u, -2.0f * kLog2e)))));
+    } else {
+        return fused_unary<OP>(v);
+    }
+}
+
+// Pairs of elements with Blackwell's packed float32 arithmetic (each lane of
+// __fadd2_rn / __fmul2_rn rounds exactly like the scalar operation; a - b is
+// a + (-b), exact in IEEE arithmetic).  The generated code uses them for chains
+// with a 16-bit output, where NaN is compared as a class.
+template <int OP>
+__device__ __forceinline__ float2 fused_binary2(float2 a, float2 b) {
+    if constexpr (OP == NODE_ADD) return __fadd2_rn(a, b);
+    else if constexpr (OP == NODE_SUB) return __fadd2_rn(a, make_float2(-b.x, -b.y));
+    else if constexpr (OP == NODE_MUL) return __fmul2_rn(a, b);
+    else return make_float2(fused_binary<OP>(a.x, b.x), fused_binary<OP>(a.y, b.y));
+}
+template <int OP>
+__device__ __forceinline__ float2 fused_unary2(float2 v) {
+    return make_float2(fused_unary<OP>(v.x), fused_unary<OP>(v.y));
+}
+// fused_unary_try on both lanes (GELU's polynomial packed).
+template <int OP>
+__device__ __forceinline__ float2 fused_unary2_try(float2 v, bool& bad) {
+    if constexpr (OP == NODE_GELU) {
+        constexpr float kM2Log2e = -2.0f * 1.4426950408889634f;
+        const float2 c3 = make_float2(0.044715f, 0.044715f), k = make_float2(0.7978845608028654f, 0.7978845608028654f);
+        const float2 u = __fmul2_rn(k, __fadd2_rn(v, __fmul2_rn(__fmul2_rn(__fmul2_rn(c3, v), v), v)));
+        const float2 a = __fmul2_rn(u, make_float2(kM2Log2e, kM2Log2e));
+        bad |= !(u.x >= -9.0f && v.x <= 3.0e38f && u.y >= -9.0f && v.y <= 3.0e38f);
+        return __fmul2_rn(v, make_float2(sfu_rcp(__fadd_rn(1.0f, sfu_ex2(a.x))), sfu_rcp(__fadd_rn(1.0f, sfu_ex2(a.y)))));
+    } else {
+        const float x = fused_unary_try<OP>(v.x, bad);
+        return make_float2(x, fused_unary_try<OP>(v.y, bad));
+    }
+}
+
 // The same with the node type known only at run time (the interpreter).
 __device__ __forceinline__ float fused_unary_rt(int op, float v) {
     switch (op) {

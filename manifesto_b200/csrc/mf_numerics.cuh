@@ -161,6 +161,18 @@ __device__ __forceinline__ uint32_t f32bits_to_f16(uint32_t u) {
     return sign | rne_shift((a & 0x7fffffu) | 0x800000u, shift);
 }
 
+// float32 x2 -> packed IEEE binary16 x2 (lo in bits 0..15): the hardware cvt
+// rounds like the reference for every non-NaN input; NaN lanes take the
+// reference's NaN rule.
+__device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    if ((lo != lo) | (hi != hi)) {
+        r = f32bits_to_f16(__float_as_uint(lo)) | (f32bits_to_f16(__float_as_uint(hi)) << 16);
+    }
+    return r;
+}
+
 // f16bitsToF32bits, dtype/float16.go:222-255: exact widening with
 // NaN -> sign | 0x7fc00000 | coef << 13.
 __device__ __forceinline__ uint32_t f16_to_f32bits(uint32_t h) {

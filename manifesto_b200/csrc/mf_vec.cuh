@@ -78,15 +78,6 @@ __device__ __forceinline__ uint32_t f32x2_to_f16x2_nonan(float lo, float hi) {
     return r;
 }
 
-// float32 x2 -> packed IEEE binary16 x2 with the reference's NaN rule.
-__device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi) {
-    uint32_t r;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-    if ((lo != lo) | (hi != hi)) {
-        r = f32bits_to_f16(__float_as_uint(lo)) | (f32bits_to_f16(__float_as_uint(hi)) << 16);
-    }
-    return r;
-}
 
 // Four float32 -> four FP8 codes (byte k = v[k]) with the hardware
 // round-to-nearest-even .satfinite conversion (OCP rule, largest finite on

@@ -170,8 +170,20 @@ def test_generated_kernel_matches_interpreter(backend, ref, seed, monkeypatch):
             assert (o[off + n * osz:] == 0xA5).all() and (o[:off] == 0xA5).all()
             outs.append((o[off:off + n * osz], fetch(am, 4, np.uint32)[0]))
             d.free(), am.free()
-        bits_equal(outs[0][0], outs[1][0])
-        assert outs[0][1] == outs[1][1]
+        if out_dt == F32:
+            # float32 outputs: both run evalCPU's rules, bit for bit
+            bits_equal(outs[0][0], outs[1][0])
+            assert outs[0][1] == outs[1][1]
+        else:
+            # 16-bit outputs: the generated code may take the float32 forms (within 1 ulp)
+            g16, i16 = (o[0].view(np.uint16) for o in outs)
+            assert ulp_diff_16(g16, i16, 0x7F80 if out_dt == BF16 else 0x7C00).max() <= 1
+        for o, am in outs:  # each kernel's amax is max|stored value| of its own output, NaN ignored
+            v = o.view({2: np.uint16, 4: np.uint32}[osz])
+            vals = ((v.astype(np.uint32) << 16).view(np.float32) if out_dt == BF16 else
+                    v.view(np.float16).astype(np.float32) if out_dt == F16 else v.view(np.float32))
+            mags = np.abs(vals[~np.isnan(vals)])
+            assert am == np.float32(mags.max() if mags.size else 0.0).view(np.uint32)
         for b in bufs:
             b.free()
     got = outs[0][0].view({2: np.uint16, 4: np.uint32}[osz])
@@ -181,6 +193,31 @@ def test_generated_kernel_matches_interpreter(backend, ref, seed, monkeypatch):
     else:
         assert ulp_diff_16(got, want, 0x7F80 if out_dt == BF16 else 0x7C00).max() <= 1
     gen.close(), interp.close()
+
+
+@pytest.mark.parametrize("out_dt", [BF16, F16])
+@pytest.mark.parametrize("op", [N.SIGMOID, N.TANH, N.GELU, N.SILU, N.EXP, N.LOG, N.SQRT])
+def test_activations_16bit_output_within_1ulp(backend, ref, op, out_dt):
+    """Each transcendental with a 16-bit output, where the generated code may use its float32 form:
+    inputs swept across every guard boundary of that form (-80, 88, GELU's u = -9, tiny and huge
+    magnitudes) plus +-0, +-Inf and NaN, all within 1 ulp of evalCPU's float64 rule; and the same
+    node under a Sub (no float32 form allowed there) as well."""
+    sweep = np.concatenate([np.linspace(-120, 120, 48001, dtype=np.float32),
+                            np.linspace(-6, -3.5, 4001, dtype=np.float32),
+                            np.float32(10.0) ** np.linspace(-38, 38, 2001, dtype=np.float32),
+                            -np.float32(10.0) ** np.linspace(-38, 38, 2001, dtype=np.float32),
+                            np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 88.0, 88.72, -80.0, -80.01], np.float32),
+                            synthetic.normal_f32(int(op) + 7, 20000, 0.0, 4.0)])
+    n = sweep.size
+    for root, label in ((fusion.unary(op, fusion.input_node(0)), "plain"),
+                        (fusion.binary(N.SUB, fusion.unary(op, fusion.input_node(0)), fusion.input_node(0)), "sub")):
+        k = fusion.emit_cuda(fusion.FusionAST(root, ["x"], "o"), out_dtype=DType(out_dt))
+        assert k.generated()
+        got, _ = run_fused(k, [sweep], n, out_dt)
+        want = ref.fused_eval(fusion.node_table(root), [sweep], [F32], [0], out_dt, n)
+        d = ulp_diff_16(got, want, 0x7F80 if out_dt == BF16 else 0x7C00)
+        assert d.max() <= 1, (label, sweep[np.argmax(d)], got[np.argmax(d)], want[np.argmax(d)])
+        k.close()
 
 
 def swiglu_inputs(n, hidden=4096, seed=synthetic.CONFIG_SEED + 40):

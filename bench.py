@@ -515,7 +515,7 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
                               "frac": round(cast_gbs / peak, 4),
                               "frac_of_direction_ceiling": round(cast_gbs / ceilings["read2_write1"]["gbs"], 4),
                               "traffic": int(tr * local_params) if tr else None},
-                "amax_pass": {"kernel": "group_amax_kernel<BF16> (read BF16)", "launch_ms": round(amax_ms, 4),
+                "amax_pass": {"kernel": "stream_amax_kernel<BF16> (read BF16)", "launch_ms": round(amax_ms, 4),
                               "gbs": round(amax_gbs, 1), "frac": round(amax_gbs / peak, 4),
                               "frac_of_direction_ceiling": round(amax_gbs / ceilings["read_only"]["gbs"], 4)},
                 "step": breakdown}

@@ -22,7 +22,10 @@
 // (16384 elements of a 16-bit source, 8192 of a float32 one) and each CTA
 // walks a contiguous range of tiles, so a
 // CTA crosses few tensor boundaries and reduces its per-tensor maximum
-// once per crossing.  Pass 1 (amax) and pass 2 (cast) are one launch each
+// once per crossing.  Pass 1 (stream_amax_kernel, one CTA per SM) has one
+// producer lane pull 32 KB tiles through a 6-stage shared-memory ring with
+// 1-D bulk copies; eight consumer warps copy a landed stage to registers,
+// release it at once and fold.  Pass 1 (amax) and pass 2 (cast) are one launch each
 // per 512 chunks; between them an NCCL max all-reduce of the amax vector
 // makes the scales global.
 #include <algorithm>
@@ -274,39 +277,6 @@ __device__ __forceinline__ int find_chunk(const AmaxArgs& a, int64_t t) {
     return lo;
 }
 
-// max|v| over one tile of one chunk (NaN ignored).
-template <int SRC>
-__device__ __forceinline__ float tile_amax(const AmaxChunk& ch, int64_t tile) {
-    using T = Tile<SRC>;
-    const int64_t c0 = tile * (T::kElems / kChunk);
-    const int64_t full = ch.n / kChunk;
-    float m = 0.0f;
-    if (ch.aligned) {
-        RawChunk<dtype_bytes(SRC)> r[T::kChunks];
-#pragma unroll
-        for (int k = 0; k < T::kChunks; ++k) {
-            const int64_t c = c0 + k * kThreads + threadIdx.x;
-            if (c < full) load_raw<dtype_bytes(SRC)>(ch.src, c, r[k]);
-        }
-        uint32_t key = 0;
-#pragma unroll
-        for (int k = 0; k < T::kChunks; ++k) {
-            const int64_t c = c0 + k * kThreads + threadIdx.x;
-            if (c < full) key = MagKey<SRC>::fold(r[k], key);
-        }
-        m = MagKey<SRC>::to_f32(key);
-        // ragged end of the chunk: the last n mod 16 elements
-        const int64_t last_tile = (ch.n - 1) / T::kElems;
-        if (tile == last_tile && threadIdx.x < (ch.n % kChunk))
-            m = fmaxf(m, abs_or_zero<SRC>(ch.src, full * kChunk + threadIdx.x));
-    } else {
-        const int64_t e0 = tile * T::kElems;
-        for (int64_t i = e0 + threadIdx.x; i < e0 + T::kElems && i < ch.n; i += kThreads)
-            m = fmaxf(m, abs_or_zero<SRC>(ch.src, i));
-    }
-    return m;
-}
-
 // This CTA's contiguous tile range [t0, t1).
 __device__ __forceinline__ void tile_range(int64_t total, int64_t& t0, int64_t& t1) {
     const int64_t per = total / gridDim.x, extra = total % gridDim.x;
@@ -315,25 +285,165 @@ __device__ __forceinline__ void tile_range(int64_t total, int64_t& t0, int64_t& 
     t1 = t0 + per + (b < extra ? 1 : 0);
 }
 
+// Pass 1 on the bulk-copy engine.  The amax fold is a few instructions per
+// 16 bytes, so the pass is bound by how many bytes are in flight: one producer
+// lane streams the CTA's tiles (32 KB each, contiguous tile ranges as above)
+// through kAmaxStages shared-memory stages -- 192 KB in flight per SM, one CTA
+// per SM, the depth at which a bare bulk-copy read reaches the DRAM read
+// ceiling -- and 256 consumer threads fold each landed tile from shared
+// memory (lane-contiguous 16-byte reads) into a per-lane magnitude key.  A
+// tensor's maximum is reduced per warp and folded into amax[tensor] with one
+// atomicMax per warp when the CTA leaves the tensor.  Every mbarrier wait is
+// bounded; a wait that runs out records MF_DEVICE_TIMEOUT.
+constexpr int kAmaxStages = 6;
+constexpr int kAmaxTileBytes = 32768;
+constexpr int kAmaxSmem = kAmaxStages * kAmaxTileBytes + 2 * kAmaxStages * 8;
+
+// Running per-lane magnitude key over one 16-byte word group (NaN never wins).
 template <int SRC>
-__global__ void __launch_bounds__(kThreads, 4) group_amax_kernel(const __grid_constant__ AmaxArgs a) {
+__device__ __forceinline__ uint32_t fold16(uint32_t key, const uint4& w) {
+    if constexpr (SRC == MF_DT_F32) {
+        const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t a = v[k] & 0x7fffffffu;
+            key = (a <= 0x7f800000u && a > key) ? a : key;
+        }
+        return key;
+    } else {
+        const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if constexpr (SRC == MF_DT_BF16) asm("max.xorsign.abs.bf16x2 %0, %0, %1;" : "+r"(key) : "r"(v[k]));
+            else asm("max.xorsign.abs.f16x2 %0, %0, %1;" : "+r"(key) : "r"(v[k]));
+        }
+        return key;
+    }
+}
+
+template <int SRC>
+__device__ __forceinline__ void flush_amax(float* amax, int tensor, uint32_t key, float mel) {
+    float m = warp_max(fmaxf(MagKey<SRC>::to_f32(key), mel));
+    if ((threadIdx.x & 31) == 0 && m > 0.0f) atomicMax(reinterpret_cast<unsigned*>(amax + tensor), __float_as_uint(m));
+}
+
+template <int SRC>
+__global__ void __launch_bounds__(kStreamBlock, 1) stream_amax_kernel(const __grid_constant__ AmaxArgs a, int* status) {
+    using T = Tile<SRC>;
+    constexpr int kIn = dtype_bytes(SRC);
+    static_assert(T::kElems * kIn == kAmaxTileBytes, "tile geometry");
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kAmaxStages * kAmaxTileBytes);
+    uint64_t* empty = full + kAmaxStages;
     int64_t t0, t1;
     tile_range(a.total_tiles, t0, t1);
     if (t0 >= t1) return;
-    int k = find_chunk(a, t0);
-    float m = 0.0f;
-    for (int64_t t = t0; t < t1; ++t) {
-        while (k + 1 < a.n_chunks && t >= a.chunk[k + 1].tile_begin) {
-            const float bm = block_max(m);
-            if (threadIdx.x == 0) atomic_max_nonneg(a.amax + a.chunk[k].tensor, bm);
-            m = 0.0f;
-            ++k;
+    const int64_t nt = t1 - t0;
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kAmaxStages; ++st) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], kConsumerWarps);
         }
-        const AmaxChunk& ch = a.chunk[k];
-        m = fmaxf(m, tile_amax<SRC>(ch, t - ch.tile_begin));
+        fence_barrier_init();
     }
-    const float bm = block_max(m);
-    if (threadIdx.x == 0) atomic_max_nonneg(a.amax + a.chunk[k].tensor, bm);
+    __syncthreads();
+    if (threadIdx.x >= kStreamThreads) {
+        if (threadIdx.x != kStreamThreads) return;
+        int k = find_chunk(a, t0);
+        int64_t i = 0;
+        bool ok = true;
+        for (; i < nt; ++i) {
+            const int st = static_cast<int>(i % kAmaxStages);
+            if (i >= kAmaxStages && !mbar_wait(&empty[st], static_cast<uint32_t>((i / kAmaxStages - 1) & 1))) {
+                ok = false;
+                break;
+            }
+            const int64_t t = t0 + i;
+            while (k + 1 < a.n_chunks && a.chunk[k + 1].tile_begin <= t) ++k;
+            const AmaxChunk& ch = a.chunk[k];
+            const int64_t e0 = (t - ch.tile_begin) * T::kElems;
+            const int64_t cnt = min(T::kElems, ch.n - e0);
+            const uint32_t bytes = static_cast<uint32_t>((cnt * kIn) & ~int64_t(15));
+            if (ch.aligned && bytes > 0) {
+                mbar_arrive_expect_tx(&full[st], bytes);
+                bulk_g2s(smem + st * kAmaxTileBytes, static_cast<const uint8_t*>(ch.src) + e0 * kIn, bytes, &full[st]);
+            } else {
+                mbar_arrive(&full[st]);
+            }
+        }
+        if (!ok) atomicExch(status, kDeviceTimeout);
+        for (int64_t j = (i > kAmaxStages ? i - kAmaxStages : 0); j < i; ++j)
+            mbar_wait(&full[j % kAmaxStages], static_cast<uint32_t>((j / kAmaxStages) & 1));
+        return;
+    }
+    const int lane = threadIdx.x & 31;
+    int k = find_chunk(a, t0);
+    int cur = a.chunk[k].tensor;
+    uint32_t key = 0;
+    float mel = 0.0f;
+    for (int64_t i = 0; i < nt; ++i) {
+        const int st = static_cast<int>(i % kAmaxStages);
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[st], static_cast<uint32_t>((i / kAmaxStages) & 1)))) {
+            if (lane == 0) atomicExch(status, kDeviceTimeout);
+            return;  // the producer's own bounded waits end the CTA
+        }
+        const int64_t t = t0 + i;
+        while (k + 1 < a.n_chunks && a.chunk[k + 1].tile_begin <= t) ++k;
+        const AmaxChunk& ch = a.chunk[k];
+        if (ch.tensor != cur) {
+            flush_amax<SRC>(a.amax, cur, key, mel);
+            cur = ch.tensor;
+            key = 0;
+            mel = 0.0f;
+        }
+        const int64_t e0 = (t - ch.tile_begin) * T::kElems;
+        const int64_t cnt = min(T::kElems, ch.n - e0);
+        if (ch.aligned && cnt == T::kElems) {
+            // pull the tile into registers and hand the stage back before folding it
+            constexpr int kV = kAmaxTileBytes / 16 / kStreamThreads;
+            const uint4* tp = reinterpret_cast<const uint4*>(smem + st * kAmaxTileBytes);
+            uint4 w[kV];
+#pragma unroll
+            for (int v = 0; v < kV; ++v) w[v] = tp[threadIdx.x + v * kStreamThreads];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+#pragma unroll
+            for (int v = 0; v < kV; ++v) key = fold16<SRC>(key, w[v]);
+            continue;
+        }
+        if (ch.aligned) {
+            const int64_t copied = (cnt * kIn) & ~int64_t(15);
+            const uint4* tp = reinterpret_cast<const uint4*>(smem + st * kAmaxTileBytes);
+            {
+                for (int v = threadIdx.x; v < copied / 16; v += kStreamThreads) key = fold16<SRC>(key, tp[v]);
+                for (int64_t e = e0 + copied / kIn + threadIdx.x; e < e0 + cnt; e += kStreamThreads)
+                    mel = fmaxf(mel, abs_or_zero<SRC>(ch.src, e));
+            }
+        } else {
+            for (int64_t e = e0 + threadIdx.x; e < e0 + cnt; e += kStreamThreads)
+                mel = fmaxf(mel, abs_or_zero<SRC>(ch.src, e));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    flush_amax<SRC>(a.amax, cur, key, mel);
+}
+
+// Launch pass 1 over one argument block (the grid is at most one CTA per SM).
+template <int SRC>
+cudaError_t launch_stream_amax(const AmaxArgs& args, int64_t tiles, cudaStream_t s) {
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(stream_amax_kernel<SRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAmaxSmem);
+        if (e != cudaSuccess) return e;
+        attr[dev] = true;
+    }
+    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, state().sm_count));
+    stream_amax_kernel<SRC><<<blocks, kStreamBlock, kAmaxSmem, s>>>(args, sticky_status_ptr());
+    return cudaGetLastError();
 }
 
 // Fill the amax / cast argument blocks with the chunks idx[first, first+count);
@@ -511,15 +621,13 @@ void group_by_dtype(const mf_chunk_desc* chunks, int32_t n_chunks, std::vector<i
 template <int SRC>
 int amax_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, float* d_amax, cudaStream_t s) {
     AmaxArgs& args = g_amax_args;
-    const int grid_cap = state().sm_count * 8;
     for (int first = 0; first < static_cast<int>(idx.size()); first += kGroupMaxChunks) {
         const int count = std::min<int>(kGroupMaxChunks, static_cast<int>(idx.size()) - first);
         args.amax = d_amax;
         const int64_t tiles = fill_amax(args, chunks, idx.data(), first, count, Tile<SRC>::kElems);
         if (tiles == 0) continue;
-        const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, grid_cap));
-        group_amax_kernel<SRC><<<blocks, kThreads, 0, s>>>(args);
-        MF_LAUNCH_CHECK("checkpoint amax pass launch");
+        const cudaError_t err = launch_stream_amax<SRC>(args, tiles, s);
+        if (err != cudaSuccess) return cuda_fail(err, "checkpoint amax pass launch");
     }
     return MF_OK;
 }
@@ -651,7 +759,6 @@ int noalloc_scratch(float** out) {
 template <int SRC>
 int noalloc_amax_launches(const mf_chunk_desc* chunks, int32_t n_chunks, float* d_amax, cudaStream_t s) {
     AmaxArgs& args = g_amax_args;
-    const int grid_cap = state().sm_count * 8;
     int32_t i = 0;
     while (i < n_chunks) {
         int count = 0;
@@ -671,9 +778,8 @@ int noalloc_amax_launches(const mf_chunk_desc* chunks, int32_t n_chunks, float* 
         args.amax = d_amax;
         args.n_chunks = count;
         args.total_tiles = tiles;
-        const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, grid_cap));
-        group_amax_kernel<SRC><<<blocks, kThreads, 0, s>>>(args);
-        MF_LAUNCH_CHECK("mf_ckpt_quant_fp8_noalloc amax pass launch");
+        const cudaError_t err = launch_stream_amax<SRC>(args, tiles, s);
+        if (err != cudaSuccess) return cuda_fail(err, "mf_ckpt_quant_fp8_noalloc amax pass launch");
     }
     return MF_OK;
 }

@@ -4,11 +4,15 @@
 Headline workload (one JSON line on rank 0): whole-checkpoint FP8 E4M3
 quantisation of a Llama-3-8B layout (291 BF16 tensors, 8,030,261,248 params,
 values N(0, 0.02)) with per-tensor amax scales, every tensor row-split over the
-N ranks (strong scaling: the checkpoint is fixed).  A step is one launch of the
-checkpoint plan (mf_ckpt_plan_run): per group of tensors an amax phase, the
-per-group amax exchanged between the ranks inside the kernel over NVLink peer
-memory, and a cast phase that re-reads the group from L2.  --path twopass times
-mf_ckpt_quant_fp8 instead (amax pass, NCCL max all-reduce, cast pass).
+N ranks (strong scaling: the checkpoint is fixed).  --path picks the step:
+  twopass  mf_ckpt_quant_fp8: amax pass, NCCL max all-reduce, cast pass
+  passes   mf_ckpt_plan_run_passes: the amax pass, whose last CTA publishes the
+           rank's maxima into every rank's exchange buffer over NVLink peer
+           memory, then the cast pass, which waits for every rank's flag inside
+           the kernel (two launches, no collective call)
+  plan     mf_ckpt_plan_run: one launch, per group of tensors an amax phase and
+           a cast phase that re-reads the group from L2, the per-group amax
+           exchanged inside the kernel
 
   value      params quantised per second, whole job (max-over-ranks device time)
   e2e        the same through the C ABI with host buffers: pinned host BF16 ->
@@ -241,7 +245,7 @@ def probe_ceiling(torch, stream_handle: int, src_ptr: int, a: int, dst_ptr: int,
             "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1), "kernel": f"bw_probe_kernel<{a},{b}>"}
 
 
-KERNEL_CONFIGS = ("c1", "c2", "c3", "c4", "c4g")
+KERNEL_CONFIGS = ("c1", "c2", "c3", "c3s", "c4", "c4g")
 
 
 def bench_kernels(torch, stream_handle: int, peak: float, which=KERNEL_CONFIGS, reps: int = 50) -> dict:
@@ -257,7 +261,8 @@ def bench_kernels(torch, stream_handle: int, peak: float, which=KERNEL_CONFIGS, 
         torch.amax(flush_words)
     out = {}
     for name in which:
-        out.update({"c1": _kernel_c1, "c2": _kernel_c2, "c3": _kernel_c3, "c4": _kernel_c4, "c4g": _kernel_c4g}[name](
+        out.update({"c1": _kernel_c1, "c2": _kernel_c2, "c3": _kernel_c3, "c3s": _kernel_c3s, "c4": _kernel_c4,
+                    "c4g": _kernel_c4g}[name](
             torch, stream_handle, peak, flush, reps))
         torch.cuda.empty_cache()
     del flush_buf
@@ -322,6 +327,27 @@ def _kernel_c3(torch, stream_handle, peak, flush, reps) -> dict:
     times = time_launches(torch, f, reps, flush)
     ceiling = probe_ceiling(torch, stream_handle, xyb.data_ptr(), 2, yb.data_ptr(), 1, n // 8, flush)
     out["c3b_axpy_bf16"] = kernel_line("axpy_vec_kernel<BF16>", 6 * n, times, peak, n, ceiling)
+    return out
+
+
+def _kernel_c3s(torch, stream_handle, peak, flush, reps) -> dict:
+    """The scalar loop beside axpy: out = x * 0.75 (applyScalarBroadcast, mul), N = 2^28, FP32 -> FP32 and
+    BF16 -> BF16 (FP32 arithmetic)."""
+    from manifesto_b200._abi import call
+    out = {}
+    n = 1 << 28
+    for key, dt, width, name in (("c3s_scalar_mul_f32", 2, 4, "F32"), ("c3s_scalar_mul_bf16", 4, 2, "BF16")):
+        src = torch.randn(n, device="cuda")
+        if width == 2:
+            src = src.to(torch.bfloat16)
+        dst = torch.empty_like(src)
+        f = lambda: call("mf_scalar_broadcast", src.data_ptr(), dt, dst.data_ptr(), dt, n, 0.75, 2, stream_handle)
+        _warm(f)
+        times = time_launches(torch, f, reps, flush)
+        ceiling = probe_ceiling(torch, stream_handle, src.data_ptr(), 1, dst.data_ptr(), 1, n * width // 16, flush)
+        out[key] = kernel_line(f"scalar_vec_kernel<{name}>", 2 * width * n, times, peak, n, ceiling)
+        del src, dst
+        torch.cuda.empty_cache()
     return out
 
 
@@ -390,7 +416,7 @@ def _kernel_c4g(torch, stream_handle, peak, flush, reps) -> dict:
     times = time_launches(torch, f, reps, flush)
     # read x, write out: the copy-shaped 1:1 mix
     ceiling = probe_ceiling(torch, stream_handle, x.data_ptr(), 1, o.data_ptr(), 1, n * 2 // 16, flush)
-    line = kernel_line("fused_interp_kernel<BF16> (Gelu(Add(Mul(x,g),b)))", 4 * n, times, peak, n, ceiling)
+    line = kernel_line("mf_jit_vec (generated for Gelu(Add(Mul(x,g),b)), BF16)", 4 * n, times, peak, n, ceiling)
     k.close()
     return {"c4g_fused_gelu_generic": line}
 
@@ -437,15 +463,17 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
         uid = dist.broadcast_bytes(checkpoint.Communicator.unique_id() if rank == 0 else None)
         comm = checkpoint.Communicator(world, rank, uid)
     plan = None
-    if args.path == "plan":
+    if args.path in ("plan", "passes"):
         plan = checkpoint.QuantPlan(chunks, len(entries), len(specs), tensor_numel=[s.numel for s in specs],
                                     group_bytes=int(args.group_mb * (1 << 20)), world=world, rank=rank)
         plan.connect(dist.all_gather_bytes(plan.ipc_handle))
         dist.barrier(torch)
 
     def step():
-        if plan is not None:
+        if args.path == "plan":
             plan.run(amax.data_ptr(), sinv.data_ptr(), stream)
+        elif args.path == "passes":
+            plan.run_passes(amax.data_ptr(), sinv.data_ptr(), stream)
         else:
             checkpoint.quantise(chunks, len(entries), len(specs), amax.data_ptr(), sinv.data_ptr(), E4M3, 0, comm,
                                 stream)
@@ -476,7 +504,24 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
                                               reps=10)}
     traffic = traffic_table()
     one_pass_bytes = 3.0 * local_params  # read BF16 once, write E4M3 once: the single-pass lower bound
-    if plan is not None:
+    passes = None
+    if args.path == "passes":
+        # the step's two launches with an event between them; the cast pass's time includes its wait for
+        # every rank's published maxima
+        passes = passes_breakdown(torch, dist, plan, amax, sinv, stream)
+        cast_x_ms = passes["cast_pass_ms"]
+        achieved = one_pass_bytes / (cast_x_ms * 1e-3) / 1e9
+        tr = traffic.get("ckpt_cast_pass")
+        roofline = {"bound": "hbm", "kernel": "stream_kernel<CastXOp<BF16,E4M3>> (waits on the ranks' published "
+                                              "amax, then reads BF16 and writes E4M3)",
+                    "alg_bytes_per_launch": int(one_pass_bytes),
+                    "launch_ms": round(cast_x_ms, 4), "achieved": round(achieved, 1), "peak": peak,
+                    "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                    "frac_of_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
+                    "traffic": int(tr * local_params) if tr else None,
+                    "direction_ceiling": ceilings["read2_write1"],
+                    "frac_of_direction_ceiling": round(achieved / ceilings["read2_write1"]["gbs"], 4)}
+    if args.path == "plan":
         # the dominant (only) kernel: the one-launch step, events around each launch
         run_ms = statistics.mean(time_launches(torch, step, 10))
         achieved = one_pass_bytes / (run_ms * 1e-3) / 1e9
@@ -561,18 +606,25 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
                        f"ckpt_fp8_e4m3_reduced_layers{args.ckpt_layers}_vocab{args.ckpt_vocab} (profiling size)",
                        "description": "whole-checkpoint per-tensor amax-scaled FP8 E4M3 quantisation, Llama-3-8B "
                                       "layout (291 BF16 tensors), rows split over ranks; "
-                                      + ("one launch per step, per-group amax exchanged between ranks inside the "
-                                         "kernel over NVLink peer memory" if args.path == "plan" else
-                                         "amax pass, NCCL max all-reduce, cast pass"),
+                                      + {"plan": "one launch per step, per-group amax exchanged between ranks "
+                                                 "inside the kernel over NVLink peer memory",
+                                         "passes": "two launches per step: the amax pass, whose last CTA "
+                                                   "publishes the rank's maxima into every rank's exchange buffer "
+                                                   "over NVLink peer memory, and the cast pass, which waits for "
+                                                   "every rank's flag inside the kernel (no collective call, no "
+                                                   "memset, no scale_inv launch)",
+                                         "twopass": "amax pass, NCCL max all-reduce, cast pass"}[args.path],
                        "path": args.path,
                        "tensors": len(specs), "params": total_params, "src_dtype": "bf16", "dst_dtype": "fp8e4m3",
                        "compat": "reference", "parallelism": f"rowsplit{world}",
                        "l2": "inputs larger than L2 (BF16 shard of 16.06 GB / N per rank)"},
             "hbm_gbs_job": round(job_gbs, 1), "alg_bytes_per_param": 3,
             "roofline": roofline, "e2e": e2e, "clocks": clocks,
-            "gpu_launches": (1 if plan is not None else 3) * args.steps,
+            "gpu_launches": {"plan": 1, "passes": 2, "twopass": 3}[args.path] * args.steps,
             "parity": parity, "two_pass": two_pass, "ceilings": ceilings,
         }
+        if passes:
+            line["passes"] = passes
         if kernels:
             line["kernels"] = kernels
         if cpu:
@@ -581,6 +633,30 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
     dist.close()
     if not parity["ok"]:
         sys.exit(3)
+
+
+def passes_breakdown(torch, dist, plan, amax, sinv, stream, reps: int = 10) -> dict:
+    """The plan's two-launch step as its two launches, a CUDA event between them, median over `reps` steps,
+    max over ranks per phase (every rank runs the same launches)."""
+    torch.cuda.synchronize()
+    dist.barrier(torch)
+    rows = []
+    for _ in range(reps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        plan.run_passes(amax.data_ptr(), sinv.data_ptr(), stream, passes=1)
+        ev[1].record()
+        plan.run_passes(amax.data_ptr(), sinv.data_ptr(), stream, passes=2)
+        ev[2].record()
+        rows.append(ev)
+    torch.cuda.synchronize()
+    out = {}
+    for k, name in enumerate(["amax_pass_ms", "cast_pass_ms"]):
+        out[name] = round(dist.max(torch, statistics.median(r[k].elapsed_time(r[k + 1]) for r in rows)), 4)
+    out["step_ms"] = round(dist.max(torch, statistics.median(r[0].elapsed_time(r[2]) for r in rows)), 4)
+    out["path"] = ("mf_ckpt_plan_run_passes: stream_amax_kernel (its last CTA publishes the rank's maxima) + "
+                   "stream_kernel<CastXOp> (waits for every rank's flag, then casts; writes amax and scale_inv)")
+    return out
 
 
 def step_breakdown(torch, dist, chunks, entries, specs, amax, sinv, comm, stream, reps: int = 10) -> dict:
@@ -834,6 +910,14 @@ def cpu_kernel_baselines(which=KERNEL_CONFIGS) -> dict:
         xb, yb = synthetic.f32_to_bf16_bits(x), synthetic.f32_to_bf16_bits(y)
         leg("c3b_axpy_bf16", n, lambda th: ref.axpy(yb.copy(), xb, 0.75, ref.BF16, threads=th),
             "axpyOntoHost bf16 over 2^24 elements (1/16 of config 3), copy of y included")
+    if "c3s" in which:
+        n = 1 << 24
+        x = synthetic.normal_f32(0x5EED0013, n)
+        leg("c3s_scalar_mul_f32", n, lambda th: ref.scalar_broadcast(x, ref.F32, ref.F32, 0.75, 2, threads=th),
+            "applyScalarBroadcast (mul) f32 over 2^24 elements (1/16 of the bench's 2^28)")
+        xb = synthetic.f32_to_bf16_bits(x)
+        leg("c3s_scalar_mul_bf16", n, lambda th: ref.scalar_broadcast(xb, ref.BF16, ref.BF16, 0.75, 2, threads=th),
+            "applyScalarBroadcast (mul) bf16 over 2^24 elements (1/16 of the bench's 2^28)")
     if "c4" in which:
         hidden, n = 4096, 1 << 22
         ins = [synthetic.normal_bf16(0x5EED0004, n), synthetic.normal_bf16(0x5EED1004, hidden, 1.0, 0.1),
@@ -903,8 +987,10 @@ def main() -> int:
                     help="comma list of per-config kernel lines to run at N=1 (c1,c2,c3,c4,c4g)")
     ap.add_argument("--only-kernels", action="store_true",
                     help="run only the per-config kernel lines (profiling); --steps sets the repetitions")
-    ap.add_argument("--path", choices=["plan", "twopass"], default="twopass",
-                    help="checkpoint step: one launch per step (mf_ckpt_plan_run) or the two-pass mf_ckpt_quant_fp8")
+    ap.add_argument("--path", choices=["plan", "passes", "twopass"], default="twopass",
+                    help="checkpoint step: the plan in one launch (mf_ckpt_plan_run), the plan in two launches with "
+                         "the amax exchange fused into them (mf_ckpt_plan_run_passes), or mf_ckpt_quant_fp8 (amax "
+                         "pass, NCCL all-reduce, cast pass)")
     ap.add_argument("--group-mb", type=float, default=32.0, help="plan: source MB per tensor group (L2 budget)")
     ap.add_argument("--ckpt-layers", type=int, default=32, help="decoder layers of the checkpoint (profiling only)")
     ap.add_argument("--ckpt-vocab", type=int, default=128256, help="vocabulary rows (profiling only)")

@@ -406,6 +406,22 @@ int mf_ckpt_plan_connect(mf_ckpt_plan plan, const void* ipc_handles);
  * d_scale_inv[n_tensors] (may be NULL) amax / fp8_max, the chunks' dst the
  * codes.  One kernel launch; no host sync. */
 int mf_ckpt_plan_run(mf_ckpt_plan plan, float* d_amax, float* d_scale_inv, mf_stream stream);
+/* The same step in two launches, with the exchange fused into them instead of
+ * a collective between them (same codes, amax and scale_inv, bit for bit):
+ *   passes & 1  the amax pass: every source byte read once, this rank's
+ *               per-tensor maxima folded into the plan's scratch; when world > 1
+ *               the launch's last CTA stores them into this rank's slot of
+ *               every rank's exchange buffer and sets its flag there (no
+ *               collective call, no memset: the scratch of a run is cleared by
+ *               the run before);
+ *   passes & 2  the cast pass: its CTAs start streaming their tiles at once,
+ *               wait (bounded) for every rank's flag of the run, take the
+ *               maximum over the slots and cast; its CTA 0 writes d_amax and
+ *               d_scale_inv (either may be NULL).
+ * passes = 3 runs both; 1 then 2 (the bench times them apart) is the same.  A
+ * run's amax pass must be followed by its cast pass before the next run, in
+ * either form (MF_ERR_INVALID_ARGUMENT otherwise).  Two launches, no host sync. */
+int mf_ckpt_plan_run_passes(mf_ckpt_plan plan, int passes, float* d_amax, float* d_scale_inv, mf_stream stream);
 int mf_ckpt_plan_info(mf_ckpt_plan plan, int32_t* n_groups, int32_t* grid, int64_t* elements);
 int mf_ckpt_plan_destroy(mf_ckpt_plan plan);
 

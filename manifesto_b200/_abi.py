@@ -104,6 +104,7 @@ SIGNATURES: dict[str, list] = {
                             ctypes.POINTER(_vp), _vp],
     "mf_ckpt_plan_connect": [_vp, _vp],
     "mf_ckpt_plan_run": [_vp, _vp, _vp, _vp],
+    "mf_ckpt_plan_run_passes": [_vp, _int, _vp, _vp, _vp],
     "mf_ckpt_plan_info": [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_i64)],
     "mf_ckpt_plan_destroy": [_vp],
 }

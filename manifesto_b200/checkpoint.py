@@ -171,6 +171,12 @@ class QuantPlan:
     def run(self, d_amax: int | None, d_scale_inv: int | None, stream=None) -> None:
         call("mf_ckpt_plan_run", self.handle, d_amax, d_scale_inv, stream_handle(stream))
 
+    def run_passes(self, d_amax: int | None, d_scale_inv: int | None, stream=None, passes: int = 3) -> None:
+        """The same step as :meth:`run` in two launches (amax pass, then the cast pass), with the amax exchange
+        done by the amax pass's last CTA (peer stores and flags) and waited for inside the cast pass.
+        ``passes`` = 1 runs only the amax pass, 2 the pending cast pass, 3 both."""
+        call("mf_ckpt_plan_run_passes", self.handle, int(passes), d_amax, d_scale_inv, stream_handle(stream))
+
     def info(self) -> dict:
         g, grid, n = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int64()
         call("mf_ckpt_plan_info", self.handle, ctypes.byref(g), ctypes.byref(grid), ctypes.byref(n))

@@ -92,11 +92,9 @@ namespace {
 #define MF_PLAN_GROUP_MB 32
 #endif
 
-constexpr int kPlanMaxWorld = 8;
 constexpr int64_t kPlanLead = MF_PLAN_LEAD;
 constexpr int kPlanCtas = MF_PLAN_CTAS;
 constexpr int64_t kDefaultGroupBytes = int64_t(MF_PLAN_GROUP_MB) << 20;
-constexpr unsigned long long kFlagWaitNs = 2000000000ull;
 
 struct PlanGroup {
     int32_t t0, t1;  // tensors [t0, t1)
@@ -121,34 +119,6 @@ struct PlanArgs {
 
 // ------------------------------------------------------------ PTX helpers
 
-__device__ __forceinline__ unsigned long long globaltimer_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
-    int32_t v;
-    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
-    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ float ld_relaxed_sys(const float* p) {
-    float v;
-    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ float ld_relaxed_gpu(const float* p) {
-    float v;
-    asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ int32_t ld_relaxed_gpu(const int32_t* p) {
-    int32_t v;
-    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -178,11 +148,6 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32
     else bulk_g2s(dst, src, bytes, bar);
 }
 
-__device__ __forceinline__ float warp_max_f32(float m) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    return m;
-}
 
 // ------------------------------------------------------- amax of a tile
 
@@ -288,9 +253,6 @@ struct ChunkCursor {
         return ch[k];
     }
 };
-
-// The 256 consumer threads of the CTA (named barrier 1; the producer warp never joins).
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kStreamThreads) : "memory"); }
 
 // Warp 0 of the CTA: wait until group g's amax is complete on every rank (one GPU:
 // every CTA of this launch has arrived; several: every rank has published).
@@ -667,14 +629,19 @@ struct mf_ckpt_plan_s {
     mf::PlanKernel kernel = nullptr;
     mf::ChunkRec* d_chunks = nullptr;
     mf::PlanGroup* d_groups = nullptr;
-    uint8_t* d_scratch = nullptr;  // local amax [2][T] | arrivals [2][G] | abandon [2]
-    size_t arrivals_off = 0, abandon_off = 0;
+    uint8_t* d_scratch = nullptr;  // local amax [2][T] | arrivals [2][G] | abandon [2], counter [2]
+    size_t arrivals_off = 0, abandon_off = 0, counter_off = 0;
     uint8_t* d_xbuf = nullptr;     // flags [G][world] | slots [2][world][T]
     size_t slots_off = 0;
     uint8_t* peer[mf::kPlanMaxWorld] = {};
     bool opened[mf::kPlanMaxWorld] = {};
     bool connected = false;
     int32_t epoch = 0;
+    // the two-launch form: the caller's chunk table, the exchange descriptor, and
+    // whether a run's amax pass is waiting for its cast pass
+    std::vector<mf_chunk_desc> table;
+    mf::AmaxXchg* d_xchg = nullptr;
+    bool pending = false;
 };
 
 using namespace mf;
@@ -689,8 +656,27 @@ void plan_release(mf_ckpt_plan_s* p) {
     cudaFree(p->d_groups);
     cudaFree(p->d_scratch);
     cudaFree(p->d_xbuf);
+    cudaFree(p->d_xchg);
     cudaGetLastError();
     delete p;
+}
+
+// The two-launch form's exchange descriptor, once every peer buffer is mapped.
+cudaError_t upload_xchg(mf_ckpt_plan_s* p) {
+    AmaxXchg h{};
+    for (int r = 0; r < p->world; ++r) {
+        h.flags[r] = reinterpret_cast<int32_t*>(p->peer[r]);
+        h.slots[r] = reinterpret_cast<float*>(p->peer[r] + p->slots_off);
+    }
+    h.local_amax = reinterpret_cast<float*>(p->d_scratch);
+    h.counter = reinterpret_cast<int32_t*>(p->d_scratch + p->counter_off);
+    h.arrivals = reinterpret_cast<int32_t*>(p->d_scratch + p->arrivals_off);
+    h.abandon = reinterpret_cast<int32_t*>(p->d_scratch + p->abandon_off);
+    h.world = p->world;
+    h.rank = p->rank;
+    h.n_tensors = p->n_tensors;
+    h.n_groups = p->n_groups;
+    return cudaMemcpy(p->d_xchg, &h, sizeof h, cudaMemcpyHostToDevice);
 }
 
 }  // namespace
@@ -832,6 +818,7 @@ extern "C" int mf_ckpt_plan_create(const mf_chunk_desc* chunks, int32_t n_chunks
         return bail(e, "mf_ckpt_plan_create: group table upload");
     p->arrivals_off = align256(sizeof(float) * 2 * n_tensors);
     p->abandon_off = p->arrivals_off + align256(sizeof(int32_t) * 2 * groups.size());
+    p->counter_off = p->abandon_off + 64;
     const size_t scratch_bytes = p->abandon_off + 256;
     if ((e = cudaMalloc(&p->d_scratch, scratch_bytes)) != cudaSuccess) return bail(e, "mf_ckpt_plan_create: scratch");
     if ((e = cudaMemset(p->d_scratch, 0, scratch_bytes)) != cudaSuccess) return bail(e, "mf_ckpt_plan_create: scratch");
@@ -854,11 +841,15 @@ extern "C" int mf_ckpt_plan_create(const mf_chunk_desc* chunks, int32_t n_chunks
     // kPlanCtas CTAs per SM (every CTA stays resident: the launch is cooperative)
     p->grid = state().sm_count * std::min(occ, kPlanCtas);
     p->peer[rank] = p->d_xbuf;
+    p->table.assign(chunks, chunks + n_chunks);
+    if ((e = cudaMalloc(&p->d_xchg, sizeof(AmaxXchg))) != cudaSuccess)
+        return bail(e, "mf_ckpt_plan_create: exchange descriptor");
     if (world > 1) {
         cudaIpcMemHandle_t h;
         if ((e = cudaIpcGetMemHandle(&h, p->d_xbuf)) != cudaSuccess) return bail(e, "mf_ckpt_plan_create: IPC handle");
         std::memcpy(ipc_handle, &h, sizeof h);
     } else {
+        if ((e = upload_xchg(p)) != cudaSuccess) return bail(e, "mf_ckpt_plan_create: exchange descriptor upload");
         p->connected = true;
     }
     *plan = p;
@@ -881,6 +872,8 @@ extern "C" int mf_ckpt_plan_connect(mf_ckpt_plan plan, const void* ipc_handles) 
         plan->peer[r] = static_cast<uint8_t*>(ptr);
         plan->opened[r] = true;
     }
+    const cudaError_t e = upload_xchg(plan);
+    if (e != cudaSuccess) return cuda_fail(e, "mf_ckpt_plan_connect: exchange descriptor upload");
     plan->connected = true;
     return MF_OK;
 }
@@ -893,6 +886,9 @@ extern "C" int mf_ckpt_plan_run(mf_ckpt_plan plan, float* d_amax, float* d_scale
                     plan->rank, plan->world - 1);
     if (plan->device != state().device)
         return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_plan_run: plan belongs to device %d", plan->device);
+    if (plan->pending)
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_plan_run: run %d's cast pass (mf_ckpt_plan_run_passes) is pending",
+                    plan->epoch);
     PlanArgs a{};
     a.chunks = plan->d_chunks;
     a.groups = plan->d_groups;
@@ -917,6 +913,34 @@ extern "C" int mf_ckpt_plan_run(mf_ckpt_plan plan, float* d_amax, float* d_scale
                                                       static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "mf_ckpt_plan_run launch");
     plan->epoch = a.epoch;
+    return MF_OK;
+}
+
+extern "C" int mf_ckpt_plan_run_passes(mf_ckpt_plan plan, int passes, float* d_amax, float* d_scale_inv,
+                                       mf_stream stream) {
+    MF_ENTER();
+    if (!plan) return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_plan_run_passes: plan is NULL");
+    if (passes < 1 || passes > 3)
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_plan_run_passes: passes must be 1 (amax), 2 (cast) or 3, got %d",
+                    passes);
+    if (!plan->connected)
+        return fail(MF_ERR_INVALID_ARGUMENT,
+                    "mf_ckpt_plan_run_passes: plan of rank %d is not connected to its %d peers", plan->rank,
+                    plan->world - 1);
+    if (plan->device != state().device)
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_plan_run_passes: plan belongs to device %d", plan->device);
+    if ((passes & 1) && plan->pending)
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_plan_run_passes: run %d's cast pass has not run", plan->epoch);
+    if (passes == 2 && !plan->pending)
+        return fail(MF_ERR_INVALID_ARGUMENT, "mf_ckpt_plan_run_passes: no amax pass to cast from (passes=1 first)");
+    const int32_t epoch = (passes & 1) ? plan->epoch + 1 : plan->epoch;
+    float* lam = reinterpret_cast<float*>(plan->d_scratch) + static_cast<int64_t>(epoch & 1) * plan->n_tensors;
+    const int rc = launch_plan_passes(plan->table.data(), static_cast<int32_t>(plan->table.size()), plan->src_dtype,
+                                      plan->d_xchg, lam, plan->world, epoch, passes, d_amax, d_scale_inv, plan->fp8,
+                                      plan->compat, static_cast<cudaStream_t>(stream));
+    if (rc) return rc;
+    plan->epoch = epoch;
+    plan->pending = passes == 1;
     return MF_OK;
 }
 

@@ -16,6 +16,14 @@ int launch_scaled_cast(const void* src, int src_dtype, void* dst, int fp8_dtype,
                        float* d_scale_inv, int64_t n, int compat, cudaStream_t s);
 // Fold max|src| into *d_amax (quant.cu).
 int launch_amax(const void* src, int src_dtype, int64_t n, float* d_amax, cudaStream_t s);
+// The two launches of a checkpoint plan's split form (quant.cu): passes bit 0
+// folds this rank's maxima into d_local_amax (the run's copy) and, world > 1,
+// publishes them through the exchange; bit 1 waits for every rank's maxima
+// and casts, the first launch writing d_amax / d_scale_inv.
+struct AmaxXchg;
+int launch_plan_passes(const mf_chunk_desc* chunks, int32_t n_chunks, int src_dtype, const AmaxXchg* d_xchg,
+                       float* d_local_amax, int world, int32_t epoch, int passes, float* d_amax, float* d_scale_inv,
+                       int fp8_dtype, int compat, cudaStream_t s);
 // In-place float32 max all-reduce over the communicator (comm.cu).
 int comm_allreduce_max(mf_comm comm, float* d_vec, int64_t count, cudaStream_t s);
 

@@ -56,12 +56,19 @@ struct ChunkRec {
     int32_t aligned;     // src and dst 16-byte aligned
 };
 
+struct AmaxXchg;
+
 template <int MaxChunks>
 struct StreamArgs {
     const float* amax;   // per-tensor amax (cast ops)
     int* status;         // sticky status word
     int64_t total_tiles;
     int32_t n_chunks;
+    int32_t epoch;       // run number of a plan's cast pass (CastXOp), else 0
+    const AmaxXchg* xchg;  // the plan's amax exchange (CastXOp), else NULL
+    float* out_amax;       // CastXOp writer launch: global amax [n_tensors] (or NULL)
+    float* out_scale_inv;  // CastXOp writer launch: scale_inv [n_tensors] (or NULL)
+    int32_t writer;        // CastXOp: this launch writes the outputs and clears the next run's scratch
     int32_t pad;
     ChunkRec chunk[MaxChunks];
 };
@@ -118,6 +125,65 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+
+// ------------------------------------------- ordering across CTAs and GPUs
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
+    int32_t v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ float ld_relaxed_sys(const float* p) {
+    float v;
+    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ float ld_relaxed_gpu(const float* p) {
+    float v;
+    asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ int32_t ld_relaxed_gpu(const int32_t* p) {
+    int32_t v;
+    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// The 256 consumer threads of the CTA (named barrier 1; the producer warp never joins).
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kStreamThreads) : "memory"); }
+
+__device__ __forceinline__ float warp_max_f32(float m) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    return m;
+}
+
+constexpr int kPlanMaxWorld = 8;                          // ranks of a checkpoint plan
+constexpr unsigned long long kFlagWaitNs = 2000000000ull;  // bound of a wait on another rank (2 s)
+
+// Per-tensor amax exchange of a checkpoint plan's two-launch form, in device
+// memory (written once when the plan is connected).  Every rank owns one
+// exchange buffer, opened by the others with CUDA IPC: flags [world] (row 0 of
+// the plan's per-group flags) and slots [2][world][n_tensors].  Pass 1's last
+// CTA stores this rank's maxima into slot (epoch & 1, rank) of every rank and
+// then releases flag `rank` there with the run's epoch; pass 2 acquires all
+// flags of its own buffer and takes the maximum over the slots.
+struct AmaxXchg {
+    float* slots[kPlanMaxWorld];    // rank r's slots (peer mappings; this rank's own buffer at [rank])
+    int32_t* flags[kPlanMaxWorld];  // rank r's flags
+    float* local_amax;              // [2][n_tensors] this rank's maxima (pass 1 folds into copy epoch & 1)
+    int32_t* counter;               // [2] CTAs of the publishing pass-1 launch that finished
+    int32_t* arrivals;              // [2][n_groups] the one-launch form's per-run scratch, cleared like it does
+    int32_t* abandon;               // [2]
+    int32_t world, rank, n_tensors, n_groups;
+};
 
 // ------------------------------------------------------------ lane steps
 //
@@ -277,6 +343,7 @@ struct ConvertOp {
     static constexpr int kLane = lane_elems<kIn, kOut>();
     static constexpr int kQ = kLane / 4;
     static constexpr bool kDefers = (DST == MF_DT_F8E4M3 || DST == MF_DT_F8E5M2) && COMPAT == 0;
+    static constexpr bool kPrologue = false;
     struct State {};
     template <class A>
     __device__ static State setup(const A&, const ChunkRec&) { return {}; }
@@ -329,6 +396,7 @@ struct CastOp {
     static constexpr int kLane = lane_elems<kIn, 1>();
     static constexpr int kQ = kLane / 4;
     static constexpr bool kDefers = COMPAT == 0;
+    static constexpr bool kPrologue = false;
     struct State {
         float scale;
     };
@@ -355,6 +423,113 @@ struct CastOp {
     __device__ static void fix(const float4& a, const float4& b, uint8_t* d) { fp8_lane_fix<FP8, kQ>(a, b, d); }
     __device__ static void element(const ChunkRec& ch, int64_t i, const State& st) {
         store_code<FP8>(ch.dst, i, encode_f32<FP8>(__fmul_rn(load_as_f32<SRC>(ch.src, i), st.scale), COMPAT));
+    }
+};
+
+// The cast pass of a checkpoint plan's two-launch form: CastOp whose scales
+// come from the plan's amax exchange instead of a finished amax vector.  Its
+// prologue (the consumer warps, before the first tile; the producer lane is
+// already streaming tiles in) waits, bounded, for every rank's flag of this
+// run, then takes each of the CTA's chunks' global amax -- the maximum over the
+// ranks' slots, or this rank's own maxima on one GPU -- into shared memory.
+// CTA 0 of the writer launch also stores the global amax and scale_inv of
+// every tensor and clears the next run's per-rank maxima and counter.  A wait
+// that runs out records MF_DEVICE_TIMEOUT and the pass completes with the
+// slots as they are (the host sees the status; no CTA waits for ever).
+template <int SRC, int FP8, int COMPAT, int MaxChunks>
+struct CastXOp : CastOp<SRC, FP8, COMPAT> {
+    using Base = CastOp<SRC, FP8, COMPAT>;
+    using State = typename Base::State;
+    static constexpr bool kPrologue = true;
+    __device__ static float* table() {
+        __shared__ float t[MaxChunks];  // global amax of chunk k0 + i
+        return t;
+    }
+    __device__ static int& first_chunk() {
+        __shared__ int k0;
+        return k0;
+    }
+    // set once the prologue is over: the producer lane streams the first ring of
+    // tiles in meanwhile, then waits for it (time-bounded like the flag waits)
+    // before its first wait for a stage to come back
+    __device__ static volatile int& ready() {
+        __shared__ int r;
+        return r;
+    }
+    __device__ static void init() { ready() = 0; }
+    __device__ static bool await_prologue() {
+        const unsigned long long start = globaltimer_ns();
+        while (!ready()) {
+            if (globaltimer_ns() - start > 2 * kFlagWaitNs) return false;
+            __nanosleep(256);
+        }
+        return true;
+    }
+    __device__ static float global_amax(const AmaxXchg& x, int par, int t) {
+        if (x.world == 1) return ld_relaxed_gpu(x.local_amax + static_cast<int64_t>(par) * x.n_tensors + t);
+        float m = 0.0f;
+        for (int r = 0; r < x.world; ++r)
+            m = fmaxf(m, ld_relaxed_sys(x.slots[x.rank] + (static_cast<int64_t>(par) * x.world + r) * x.n_tensors + t));
+        return m;
+    }
+    template <class A>
+    __device__ static void prologue(const A& a, int64_t t0, int64_t t1) {
+        const AmaxXchg& x = *a.xchg;
+        const int par = a.epoch & 1;
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        if (x.world > 1 && warp == 0) {
+            bool ok = true;
+            if (lane < x.world) {
+                const int32_t* f = x.flags[x.rank] + lane;
+                const unsigned long long start = globaltimer_ns();
+                // flags only grow; "at least this epoch"
+                while (static_cast<int32_t>(static_cast<uint32_t>(ld_acquire_sys(f)) - static_cast<uint32_t>(a.epoch)) < 0) {
+                    if (globaltimer_ns() - start > kFlagWaitNs) {
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            if (!__all_sync(0xffffffffu, ok) && lane == 0) atomicExch(a.status, kDeviceTimeout);
+        }
+        consumers_sync();
+        if (t0 < t1) {
+            // the chunks of tiles [t0, t1): one warp per chunk
+            int k0 = 0, k1 = a.n_chunks - 1;
+            while (k0 < k1) {
+                const int mid = (k0 + k1 + 1) >> 1;
+                if (a.chunk[mid].tile_begin <= t0) k0 = mid;
+                else k1 = mid - 1;
+            }
+            k1 = k0;
+            while (k1 + 1 < a.n_chunks && a.chunk[k1 + 1].tile_begin < t1) ++k1;
+            if (threadIdx.x == 0) first_chunk() = k0;
+            for (int k = k0 + warp; k <= k1; k += kConsumerWarps)
+                if (lane == 0) table()[k - k0] = global_amax(x, par, a.chunk[k].tensor);
+        }
+        if (blockIdx.x == 0 && a.writer) {
+            float* next = x.local_amax + static_cast<int64_t>(par ^ 1) * x.n_tensors;
+            for (int t = threadIdx.x; t < x.n_tensors; t += kStreamThreads) {
+                const float g = global_amax(x, par, t);
+                if (a.out_amax) a.out_amax[t] = g;
+                if (a.out_scale_inv) a.out_scale_inv[t] = scale_inv_from_amax(g, FP8);
+                next[t] = 0.0f;
+            }
+            for (int g = threadIdx.x; g < x.n_groups; g += kStreamThreads)
+                x.arrivals[static_cast<int64_t>(par ^ 1) * x.n_groups + g] = 0;
+            if (threadIdx.x == 0) {
+                x.counter[par ^ 1] = 0;
+                x.abandon[par ^ 1] = 0;
+            }
+        }
+        consumers_sync();
+        if (threadIdx.x == 0) ready() = 1;
+    }
+    template <class A>
+    __device__ static State setup(const A& a, const ChunkRec& ch) {
+        const int k = static_cast<int>(&ch - a.chunk);
+        return {scale_from_amax(table()[k - first_chunk()], FP8)};
     }
 };
 
@@ -408,7 +583,12 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
     const int64_t b = blockIdx.x;
     const int64_t t0 = b * per + (b < extra ? b : extra);
     const int64_t t1 = t0 + per + (b < extra ? 1 : 0);
-    if (t0 >= t1) return;
+    if (t0 >= t1) {
+        // a CTA without tiles still takes part in the op's prologue (CTA 0 may be its writer)
+        if constexpr (Op::kPrologue)
+            if (threadIdx.x < kStreamThreads) Op::prologue(a, t0, t1);
+        return;
+    }
     const int64_t ntiles = t1 - t0;
 
     if (threadIdx.x == 0) {
@@ -417,6 +597,7 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
             mbar_init(&empty[s], kConsumerWarps);
         }
         fence_barrier_init();
+        if constexpr (Op::kPrologue) Op::init();
     }
     __syncthreads();
 
@@ -428,6 +609,12 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
         bool ok = true;
         for (; i < ntiles; ++i) {
             const int s = static_cast<int>(i % G::kStages);
+            if constexpr (Op::kPrologue) {
+                if (i == G::kStages && !Op::await_prologue()) {
+                    ok = false;
+                    break;
+                }
+            }
             if (i >= G::kStages &&
                 !mbar_wait(&empty[s], static_cast<uint32_t>((i / G::kStages - 1) & 1))) {
                 ok = false;
@@ -463,6 +650,7 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
            (threadIdx.x >> 5) * kFixSlots;
     fq.n = 0;
     fq.age = 0;
+    if constexpr (Op::kPrologue) Op::prologue(a, t0, t1);
     int k = stream_first_chunk(a, t0);
     typename Op::State st = Op::setup(a, a.chunk[k]);
     for (int64_t i = 0; i < ntiles; ++i) {
@@ -547,7 +735,10 @@ inline cudaError_t launch_stream(const StreamArgs<MaxChunks>& a, int sm_count, c
     if (MaxChunks > 1 && resident > 2) resident = 2;
     int64_t blocks = static_cast<int64_t>(sm_count) * resident;
     if (a.total_tiles < blocks) blocks = a.total_tiles;
-    if (blocks < 1) return cudaSuccess;
+    if (blocks < 1) {
+        if constexpr (!Op::kPrologue) return cudaSuccess;
+        blocks = 1;  // the prologue still runs (CTA 0 may be the writer)
+    }
     stream_kernel<Op, MaxChunks><<<static_cast<unsigned>(blocks), kStreamBlock, G::kSmemBytes, s>>>(a);
     return cudaGetLastError();
 }

@@ -263,6 +263,9 @@ struct AmaxArgs {
     float* amax;
     int64_t total_tiles;
     int32_t n_chunks;
+    int32_t publish;        // the launch's last CTA publishes `amax` through xchg (a plan's two-launch form)
+    const AmaxXchg* xchg;
+    int32_t epoch;
     int32_t pad;
     AmaxChunk chunk[kGroupMaxChunks];
 };
@@ -327,6 +330,32 @@ __device__ __forceinline__ void flush_amax(float* amax, int tensor, uint32_t key
     if ((threadIdx.x & 31) == 0 && m > 0.0f) atomicMax(reinterpret_cast<unsigned*>(amax + tensor), __float_as_uint(m));
 }
 
+// Warp 0 of every CTA of a publishing pass-1 launch, once the CTA's maxima are
+// folded into a.amax: the last CTA to arrive stores this rank's maxima into
+// its slot of every rank's exchange buffer (plain stores into peer memory
+// opened with CUDA IPC; no multicast) and then releases its flag there with
+// the run's epoch.
+__device__ void amax_publish(const AmaxArgs& a) {
+    const AmaxXchg& x = *a.xchg;
+    const int lane = threadIdx.x & 31;
+    const int par = a.epoch & 1;
+    int last = 0;
+    if (lane == 0) {
+        __threadfence();
+        last = atomicAdd(x.counter + par, 1) == static_cast<int>(gridDim.x) - 1;
+    }
+    if (!__shfl_sync(0xffffffffu, last, 0)) return;
+    __threadfence();
+    if (lane == 0) x.counter[par] = 0;
+    for (int r = 0; r < x.world; ++r) {
+        float* dst = x.slots[r] + (static_cast<int64_t>(par) * x.world + x.rank) * x.n_tensors;
+        for (int t = lane; t < x.n_tensors; t += 32) dst[t] = ld_relaxed_gpu(a.amax + t);
+    }
+    __threadfence_system();
+    __syncwarp();
+    if (lane < x.world) st_release_sys(x.flags[lane] + x.rank, a.epoch);
+}
+
 template <int SRC>
 __global__ void __launch_bounds__(kStreamBlock, 1) stream_amax_kernel(const __grid_constant__ AmaxArgs a, int* status) {
     using T = Tile<SRC>;
@@ -337,7 +366,10 @@ __global__ void __launch_bounds__(kStreamBlock, 1) stream_amax_kernel(const __gr
     uint64_t* empty = full + kAmaxStages;
     int64_t t0, t1;
     tile_range(a.total_tiles, t0, t1);
-    if (t0 >= t1) return;
+    if (t0 >= t1) {
+        if (a.publish && threadIdx.x < 32) amax_publish(a);
+        return;
+    }
     const int64_t nt = t1 - t0;
     if (threadIdx.x == 0) {
         for (int st = 0; st < kAmaxStages; ++st) {
@@ -385,7 +417,7 @@ __global__ void __launch_bounds__(kStreamBlock, 1) stream_amax_kernel(const __gr
         const int st = static_cast<int>(i % kAmaxStages);
         if (!__all_sync(0xffffffffu, mbar_wait(&full[st], static_cast<uint32_t>((i / kAmaxStages) & 1)))) {
             if (lane == 0) atomicExch(status, kDeviceTimeout);
-            return;  // the producer's own bounded waits end the CTA
+            break;  // the producer's own bounded waits end its loop; the warp still meets the CTA below
         }
         const int64_t t = t0 + i;
         while (k + 1 < a.n_chunks && a.chunk[k + 1].tile_begin <= t) ++k;
@@ -427,6 +459,11 @@ __global__ void __launch_bounds__(kStreamBlock, 1) stream_amax_kernel(const __gr
         if (lane == 0) mbar_arrive(&empty[st]);
     }
     flush_amax<SRC>(a.amax, cur, key, mel);
+    if (a.publish) {
+        __threadfence();   // this warp's atomicMax results before the CTA's ticket
+        consumers_sync();
+        if (threadIdx.x < 32) amax_publish(a);
+    }
 }
 
 // Launch pass 1 over one argument block (the grid is at most one CTA per SM).
@@ -441,7 +478,8 @@ cudaError_t launch_stream_amax(const AmaxArgs& args, int64_t tiles, cudaStream_t
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
-    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(tiles, state().sm_count));
+    // a publishing launch runs even without tiles (its one CTA publishes zeros)
+    const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(tiles, state().sm_count)));
     stream_amax_kernel<SRC><<<blocks, kStreamBlock, kAmaxSmem, s>>>(args, sticky_status_ptr());
     return cudaGetLastError();
 }
@@ -624,6 +662,7 @@ int amax_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, 
     for (int first = 0; first < static_cast<int>(idx.size()); first += kGroupMaxChunks) {
         const int count = std::min<int>(kGroupMaxChunks, static_cast<int>(idx.size()) - first);
         args.amax = d_amax;
+        args.publish = 0;
         const int64_t tiles = fill_amax(args, chunks, idx.data(), first, count, Tile<SRC>::kElems);
         if (tiles == 0) continue;
         const cudaError_t err = launch_stream_amax<SRC>(args, tiles, s);
@@ -677,7 +716,108 @@ int launch_cast_pass(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_te
     if (!rc) rc = cast_launches<MF_DT_F32>(chunks, by[2], d_amax, fp8_dtype, compat, s);
     return rc;
 }
+
+// ---- a checkpoint plan's two-launch form (one source dtype per plan)
+
+// Pass 1 into this run's copy of the per-rank maxima; with several ranks the
+// last launch publishes them (it runs, as one CTA, even when this rank holds
+// no elements, so that the other ranks are never left waiting).
+template <int SRC>
+int plan_amax_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, const AmaxXchg* xchg,
+                       float* lam, int world, int32_t epoch, cudaStream_t s) {
+    AmaxArgs& args = g_amax_args;
+    const int n = static_cast<int>(idx.size());
+    int first = 0;
+    do {
+        const int count = std::min<int>(kGroupMaxChunks, n - first);
+        args.amax = lam;
+        args.xchg = xchg;
+        args.epoch = epoch;
+        const int64_t tiles = fill_amax(args, chunks, idx.data(), first, count, Tile<SRC>::kElems);
+        args.publish = (world > 1 && first + count >= n) ? 1 : 0;
+        if (tiles > 0 || args.publish) {
+            const cudaError_t err = launch_stream_amax<SRC>(args, tiles, s);
+            if (err != cudaSuccess) return cuda_fail(err, "checkpoint plan amax pass launch");
+        }
+        first += count;
+    } while (first < n);
+    return MF_OK;
+}
+
+// Pass 2: the cast with the exchange in its prologue; the first launch is the
+// writer of the amax / scale_inv outputs (it runs even without tiles).
+template <int SRC, int FP8, int COMPAT>
+int plan_cast_launches(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, const AmaxXchg* xchg,
+                       int32_t epoch, float* d_amax, float* d_scale_inv, cudaStream_t s) {
+    StreamArgs<kGroupMaxChunks>& args = g_cast_args;
+    const int n = static_cast<int>(idx.size());
+    int first = 0;
+    do {
+        const int count = std::min<int>(kGroupMaxChunks, n - first);
+        args.amax = nullptr;
+        args.status = sticky_status_ptr();
+        args.xchg = xchg;
+        args.epoch = epoch;
+        args.out_amax = d_amax;
+        args.out_scale_inv = d_scale_inv;
+        args.writer = first == 0 ? 1 : 0;
+        const int64_t tiles = fill_cast(args, chunks, idx.data(), first, count, stream_tile_elems<dtype_bytes(SRC)>());
+        if (tiles > 0 || args.writer) {
+            const cudaError_t err =
+                launch_stream<CastXOp<SRC, FP8, COMPAT, kGroupMaxChunks>, kGroupMaxChunks>(args, state().sm_count, s);
+            if (err != cudaSuccess) return cuda_fail(err, "checkpoint plan cast pass launch");
+        }
+        first += count;
+    } while (first < n);
+    return MF_OK;
+}
+
+template <int SRC>
+int plan_cast_dispatch(const mf_chunk_desc* chunks, const std::vector<int32_t>& idx, const AmaxXchg* xchg,
+                       int32_t epoch, float* d_amax, float* d_scale_inv, int fp8_dtype, int compat, cudaStream_t s) {
+    if (fp8_dtype == MF_DT_F8E4M3)
+        return compat ? plan_cast_launches<SRC, MF_DT_F8E4M3, 1>(chunks, idx, xchg, epoch, d_amax, d_scale_inv, s)
+                      : plan_cast_launches<SRC, MF_DT_F8E4M3, 0>(chunks, idx, xchg, epoch, d_amax, d_scale_inv, s);
+    return compat ? plan_cast_launches<SRC, MF_DT_F8E5M2, 1>(chunks, idx, xchg, epoch, d_amax, d_scale_inv, s)
+                  : plan_cast_launches<SRC, MF_DT_F8E5M2, 0>(chunks, idx, xchg, epoch, d_amax, d_scale_inv, s);
+}
 }  // namespace
+
+namespace mf {
+int launch_plan_passes(const mf_chunk_desc* chunks, int32_t n_chunks, int src_dtype, const AmaxXchg* d_xchg,
+                       float* d_local_amax, int world, int32_t epoch, int passes, float* d_amax, float* d_scale_inv,
+                       int fp8_dtype, int compat, cudaStream_t s) {
+    std::lock_guard<std::mutex> lock(g_group_mutex);
+    std::vector<int32_t> idx;
+    for (int32_t i = 0; i < n_chunks; ++i)
+        if (chunks[i].n > 0) idx.push_back(i);
+    int rc = MF_OK;
+    if (passes & 1) {
+        switch (src_dtype) {
+        case MF_DT_BF16: rc = plan_amax_launches<MF_DT_BF16>(chunks, idx, d_xchg, d_local_amax, world, epoch, s); break;
+        case MF_DT_F16: rc = plan_amax_launches<MF_DT_F16>(chunks, idx, d_xchg, d_local_amax, world, epoch, s); break;
+        case MF_DT_F32: rc = plan_amax_launches<MF_DT_F32>(chunks, idx, d_xchg, d_local_amax, world, epoch, s); break;
+        default: return fail(MF_ERR_DTYPE_UNSUPPORTED, "checkpoint plan: source dtype %d unsupported", src_dtype);
+        }
+        if (rc) return rc;
+    }
+    if (passes & 2) {
+        switch (src_dtype) {
+        case MF_DT_BF16:
+            rc = plan_cast_dispatch<MF_DT_BF16>(chunks, idx, d_xchg, epoch, d_amax, d_scale_inv, fp8_dtype, compat, s);
+            break;
+        case MF_DT_F16:
+            rc = plan_cast_dispatch<MF_DT_F16>(chunks, idx, d_xchg, epoch, d_amax, d_scale_inv, fp8_dtype, compat, s);
+            break;
+        case MF_DT_F32:
+            rc = plan_cast_dispatch<MF_DT_F32>(chunks, idx, d_xchg, epoch, d_amax, d_scale_inv, fp8_dtype, compat, s);
+            break;
+        default: return fail(MF_ERR_DTYPE_UNSUPPORTED, "checkpoint plan: source dtype %d unsupported", src_dtype);
+        }
+    }
+    return rc;
+}
+}  // namespace mf
 
 extern "C" int mf_ckpt_amax_pass(const mf_chunk_desc* chunks, int32_t n_chunks, int32_t n_tensors, float* d_amax,
                                  mf_stream stream) {
@@ -776,6 +916,7 @@ int noalloc_amax_launches(const mf_chunk_desc* chunks, int32_t n_chunks, float* 
         }
         if (count == 0) continue;
         args.amax = d_amax;
+        args.publish = 0;
         args.n_chunks = count;
         args.total_tiles = tiles;
         const cudaError_t err = launch_stream_amax<SRC>(args, tiles, s);

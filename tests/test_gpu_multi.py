@@ -4,8 +4,10 @@ One process per GPU; each quantises its row range of every tensor with
 mf_ckpt_quant_fp8 and the NCCL max all-reduce of the amax vector between the
 two passes.  The shards, put back together, must equal the CPU oracle's
 single-process quantisation bit for bit; mf_ckpt_quant_fp8_noalloc over the
-same communicator, and the one-launch plan (its amax exchanged inside the
-kernel through the two GPUs' exchange buffers), must give the same bytes.  NCCL runs with its defaults, as
+same communicator, and the checkpoint plan in both forms (one launch, its
+amax exchanged inside the kernel; two launches, the amax published by pass 1
+and waited for inside pass 2; both through the two GPUs' exchange buffers),
+must give the same bytes.  NCCL runs with its defaults, as
 in bench.py.  Skipped with fewer than 2 GPUs.
 """
 import os
@@ -88,6 +90,23 @@ def _rank_main(rank: int, port: int, out_dir: str) -> None:
         plan_same &= all(np.array_equal(fetch(d, n), o) for d, n, o in zip(pl_dsts, sizes, out))
         plan_same &= np.array_equal(fetch(pl_si, 4 * len(specs)), fetch(si, 4 * len(specs)))
         plan_same &= np.array_equal(fetch(pl_am, 4 * len(specs)), fetch(am, 4 * len(specs)))
+    # the plan's two-launch form (amax published by pass 1's last CTA, waited for inside the cast pass):
+    # outputs cleared before every run, four runs, the first three in a row with no barrier between ranks
+    for k in range(4):
+        for d, n in zip(pl_dsts, sizes):
+            d.upload(np.zeros(n, np.uint8))
+        if k % 2:
+            plan.run_passes(pl_am.ptr, pl_si.ptr, passes=1)
+            plan.run_passes(pl_am.ptr, pl_si.ptr, passes=2)
+        else:
+            plan.run_passes(pl_am.ptr, pl_si.ptr)
+        sync_device()
+        plan_same &= all(np.array_equal(fetch(d, n), o) for d, n, o in zip(pl_dsts, sizes, out))
+        plan_same &= np.array_equal(fetch(pl_si, 4 * len(specs)), fetch(si, 4 * len(specs)))
+        plan_same &= np.array_equal(fetch(pl_am, 4 * len(specs)), fetch(am, 4 * len(specs)))
+    plan.run(pl_am.ptr, pl_si.ptr)  # and the one-launch form again after them
+    sync_device()
+    plan_same &= all(np.array_equal(fetch(d, n), o) for d, n, o in zip(pl_dsts, sizes, out))
     # every rank's last run has finished before any exchange buffer is freed
     store.add("plan_done", 1)
     deadline = time.time() + 60

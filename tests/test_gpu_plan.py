@@ -1,4 +1,5 @@
-"""The checkpoint step in one launch (mf_ckpt_plan_*, checkpoint.QuantPlan) on one GPU.
+"""The checkpoint plan (mf_ckpt_plan_*, checkpoint.QuantPlan) on one GPU: the step in one launch and in
+two launches with the exchange fused into them (mf_ckpt_plan_run_passes).
 
 Every run is checked bit for bit against the CPU oracle (amax, scale_inv and the FP8
 codes of every tensor) and against the two-pass mf_ckpt_quant_fp8 on the same table.
@@ -47,10 +48,25 @@ def _check(ref, raws, dts, dsts, ns, amax, sinv, fp8, compat=0):
             bits_equal(fetch(dsts[t], ns[t]), ref.scaled_cast(raw, dt, fp8, a, compat=compat))
 
 
+def _run(plan, form, run, am, si):
+    """One step in the named form: "one" the one-launch kernel, "passes" the two-launch form (passes=3, or
+    1 then 2 on odd runs), "mixed" alternating the two forms on one plan."""
+    if form == "one" or (form == "mixed" and run % 2 == 0):
+        plan.run(am, si)
+    elif run % 2:
+        plan.run_passes(am, si, passes=1)
+        plan.run_passes(am, si, passes=2)
+    else:
+        plan.run_passes(am, si)
+
+
+@pytest.mark.parametrize("form", ["one", "passes", "mixed"])
 @pytest.mark.parametrize("group_bytes", [0, 200_000, 1])
-def test_plan_runs_in_a_row_match_oracle_and_two_pass(backend, ref, group_bytes):
+def test_plan_runs_in_a_row_match_oracle_and_two_pass(backend, ref, group_bytes, form):
     """Three runs on one plan, the data replaced between them (sigma 0.5, 0.005, 0.05): every run
-    exact; one group for the whole table, many groups, and one group per tensor."""
+    exact; one group for the whole table, many groups, and one group per tensor; in the one-launch
+    form, the two-launch form, and both alternating on one plan (each form clears the other's
+    per-run scratch)."""
     specs = _layout()
     n = [s.numel for s in specs]
     srcs = [empty(2 * k) for k in n]
@@ -69,7 +85,9 @@ def test_plan_runs_in_a_row_match_oracle_and_two_pass(backend, ref, group_bytes)
         raws = [_raw(9000 + 100 * run + t, k, BF16, sigma * (1 + t % 5)) for t, k in enumerate(n)]
         for s, r in zip(srcs, raws):
             s.upload(r)
-        plan.run(am.ptr, si.ptr)
+        for d in dsts:
+            d.upload(np.zeros(d.nbytes, np.uint8))
+        _run(plan, form, run, am.ptr, si.ptr)
         checkpoint.quantise(ref_chunks, len(n), len(n), ram.ptr, rsi.ptr)
         _check(ref, raws, [BF16] * len(n), dsts, n, am, si, E4M3)
         for d, r in zip(dsts, ref_dsts):
@@ -80,8 +98,9 @@ def test_plan_runs_in_a_row_match_oracle_and_two_pass(backend, ref, group_bytes)
         b.free()
 
 
+@pytest.mark.parametrize("form", ["one", "passes"])
 @pytest.mark.parametrize("src_dt,fp8,compat", [(F16, E4M3, 0), (F32, E5M2, 0), (BF16, E5M2, 1), (F32, E4M3, 1)])
-def test_plan_source_dtypes_ragged_split_chunks(backend, ref, src_dt, fp8, compat):
+def test_plan_source_dtypes_ragged_split_chunks(backend, ref, src_dt, fp8, compat, form):
     """F16 / F32 / BF16 sources, both FP8 formats, both compat modes; ragged sizes, a tensor split
     into chunks that leave the second off 16-byte alignment, an empty chunk, a tensor with no
     chunk at all (its amax 0, scale_inv 1), many small groups."""
@@ -105,8 +124,8 @@ def test_plan_source_dtypes_ragged_split_chunks(backend, ref, src_dt, fp8, compa
                                 group_bytes=60_000, fp8_dtype=DType(fp8), compat=compat)
     assert plan.info()["groups"] > 2
     am, si = empty(4 * len(sizes)), empty(4 * len(sizes))
-    for _ in range(2):
-        plan.run(am.ptr, si.ptr)
+    for run in range(2):
+        _run(plan, form, run, am.ptr, si.ptr)
     _check(ref, raws, [src_dt] * len(sizes), dsts, sizes, am, si, fp8, compat)
     plan.close()
     for b in srcs + dsts + [am, si]:
@@ -127,6 +146,21 @@ def test_plan_rejects(backend):
     with pytest.raises(InvalidArgument, match="ipc_handle"):
         call("mf_ckpt_plan_create", one, 1, 1, None, 0, 2, 0, int(DType.FLOAT8_E4M3), 0,
              ctypes.byref(ctypes.c_void_p()), None)
+    # the two-launch form: a run's amax pass, then its cast pass, before anything else
+    plan = checkpoint.QuantPlan(one, 1, 1)
+    for bad in (0, 4):
+        with pytest.raises(InvalidArgument, match="passes must be"):
+            plan.run_passes(None, None, passes=bad)
+    with pytest.raises(InvalidArgument, match="no amax pass"):
+        plan.run_passes(None, None, passes=2)
+    plan.run_passes(None, None, passes=1)
+    with pytest.raises(InvalidArgument, match="cast pass has not run"):
+        plan.run_passes(None, None, passes=1)
+    with pytest.raises(InvalidArgument, match="pending"):
+        plan.run(None, None)
+    plan.run_passes(None, None, passes=2)
+    plan.run(None, None)
+    plan.close()
     a.free(), b.free()
 
 
@@ -148,10 +182,12 @@ def _silent_peer(port: int, ready, done) -> None:
     plan.close()
 
 
-def test_plan_peer_that_never_runs_times_out(backend, ref):
+@pytest.mark.parametrize("form", ["one", "passes"])
+def test_plan_peer_that_never_runs_times_out(backend, ref, form):
     """A two-rank plan whose other rank connects but never launches: this rank's wait for the
     peer's amax runs out after its bound (~2 s), the run reports MF_DEVICE_TIMEOUT through the
-    sticky status instead of hanging, and the context stays usable."""
+    sticky status instead of hanging, and the context stays usable.  In the two-launch form the
+    amax pass publishes into the peer's buffer and the cast pass's waits run out."""
     import datetime
     import socket
 
@@ -174,7 +210,10 @@ def test_plan_peer_that_never_runs_times_out(backend, ref):
         plan.connect_via_store(store)  # returns once the peer has published its handle
         assert ready.wait(120), "peer did not come up"
         assert status() == 0
-        plan.run(am.ptr, si.ptr)
+        if form == "one":
+            plan.run(am.ptr, si.ptr)
+        else:
+            plan.run_passes(am.ptr, si.ptr)
         assert status() == MF_DEVICE_TIMEOUT
         plan.close()  # unmaps the peer's buffer before the peer frees it
         done.set()

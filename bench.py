@@ -4,7 +4,8 @@
 Headline workload (one JSON line on rank 0): whole-checkpoint FP8 E4M3
 quantisation of a Llama-3-8B layout (291 BF16 tensors, 8,030,261,248 params,
 values N(0, 0.02)) with per-tensor amax scales, every tensor row-split over the
-N ranks (strong scaling: the checkpoint is fixed).  --path picks the step:
+N ranks (strong scaling: the checkpoint is fixed).  --path picks the step
+(default auto: twopass on one GPU, passes on several):
   twopass  mf_ckpt_quant_fp8: amax pass, NCCL max all-reduce, cast pass
   passes   mf_ckpt_plan_run_passes: the amax pass, whose last CTA publishes the
            rank's maxima into every rank's exchange buffer over NVLink peer
@@ -319,14 +320,14 @@ def _kernel_c3(torch, stream_handle, peak, flush, reps) -> dict:
     times = time_launches(torch, f, reps, flush)
     xyb = xy.to(torch.bfloat16)
     ceiling = probe_ceiling(torch, stream_handle, xy.data_ptr(), 2, y.data_ptr(), 1, n // 4, flush)
-    out["c3a_axpy_f32"] = kernel_line("axpy_vec_kernel<F32>", 12 * n, times, peak, n, ceiling)
+    out["c3a_axpy_f32"] = kernel_line("stream_kernel<AxpyOp<F32>>", 12 * n, times, peak, n, ceiling)
     del xy, x, y
     xb, yb = xyb[:n], xyb[n:]
     f = lambda: call("mf_axpy", yb.data_ptr(), xb.data_ptr(), n, 0.75, 4, 0, stream_handle)
     _warm(f)
     times = time_launches(torch, f, reps, flush)
     ceiling = probe_ceiling(torch, stream_handle, xyb.data_ptr(), 2, yb.data_ptr(), 1, n // 8, flush)
-    out["c3b_axpy_bf16"] = kernel_line("axpy_vec_kernel<BF16>", 6 * n, times, peak, n, ceiling)
+    out["c3b_axpy_bf16"] = kernel_line("stream_kernel<AxpyOp<BF16>>", 6 * n, times, peak, n, ceiling)
     return out
 
 
@@ -336,7 +337,7 @@ def _kernel_c3s(torch, stream_handle, peak, flush, reps) -> dict:
     from manifesto_b200._abi import call
     out = {}
     n = 1 << 28
-    for key, dt, width, name in (("c3s_scalar_mul_f32", 2, 4, "F32"), ("c3s_scalar_mul_bf16", 4, 2, "BF16")):
+    for key, dt, width, name in (("c3s_scalar_mul_f32", 2, 4, "F32,F32"), ("c3s_scalar_mul_bf16", 4, 2, "BF16,BF16")):
         src = torch.randn(n, device="cuda")
         if width == 2:
             src = src.to(torch.bfloat16)
@@ -345,7 +346,7 @@ def _kernel_c3s(torch, stream_handle, peak, flush, reps) -> dict:
         _warm(f)
         times = time_launches(torch, f, reps, flush)
         ceiling = probe_ceiling(torch, stream_handle, src.data_ptr(), 1, dst.data_ptr(), 1, n * width // 16, flush)
-        out[key] = kernel_line(f"scalar_vec_kernel<{name}>", 2 * width * n, times, peak, n, ceiling)
+        out[key] = kernel_line(f"stream_kernel<ScalarOp<{name},mul>>", 2 * width * n, times, peak, n, ceiling)
         del src, dst
         torch.cuda.empty_cache()
     return out
@@ -441,6 +442,8 @@ def run_ours(args, world: int, rank: int, local_rank: int) -> None:
         dist.close()
         return
 
+    if args.path == "auto":
+        args.path = "twopass" if world == 1 else "passes"
     full = args.ckpt_layers == 32 and args.ckpt_vocab == 128256
     specs = checkpoint.llama3_8b_layout(layers=args.ckpt_layers, vocab=args.ckpt_vocab)
     total_params = sum(s.numel for s in specs)
@@ -987,10 +990,11 @@ def main() -> int:
                     help="comma list of per-config kernel lines to run at N=1 (c1,c2,c3,c4,c4g)")
     ap.add_argument("--only-kernels", action="store_true",
                     help="run only the per-config kernel lines (profiling); --steps sets the repetitions")
-    ap.add_argument("--path", choices=["plan", "passes", "twopass"], default="twopass",
+    ap.add_argument("--path", choices=["auto", "plan", "passes", "twopass"], default="auto",
                     help="checkpoint step: the plan in one launch (mf_ckpt_plan_run), the plan in two launches with "
                          "the amax exchange fused into them (mf_ckpt_plan_run_passes), or mf_ckpt_quant_fp8 (amax "
-                         "pass, NCCL all-reduce, cast pass)")
+                         "pass, NCCL all-reduce, cast pass); auto: twopass on one GPU (nothing to exchange), passes "
+                         "on several")
     ap.add_argument("--group-mb", type=float, default=32.0, help="plan: source MB per tensor group (L2 budget)")
     ap.add_argument("--ckpt-layers", type=int, default=32, help="decoder layers of the checkpoint (profiling only)")
     ap.add_argument("--ckpt-vocab", type=int, default=128256, help="vocabulary rows (profiling only)")

@@ -8,10 +8,14 @@
 // build does not contract), or one fused rounding when fused_fma is set.
 // mf_scalar_broadcast replaces applyScalarBroadcast
 // (runtime/executor_math.go:195-234) plus its store encode.
-// Both work on lane-contiguous quads (4 elements per lane per access).
-// Roofline: HBM; axpy moves 3 * sizeof(dtype) bytes per element.
+// With 16-byte aligned buffers both run on the bulk-copy streaming engine
+// (mf_stream.cuh): axpy as a two-source op (y and x staged side by side in
+// every stage, y written back in place), the scalar op as a one-source op;
+// unaligned buffers take per-element kernels with the same arithmetic.
+// Roofline: HBM; axpy moves 3 * sizeof(dtype) bytes per element, the scalar
+// op src + dst bytes.
 #include "mf_runtime.h"
-#include "mf_vec.cuh"
+#include "mf_stream.cuh"
 
 namespace mf {
 namespace {
@@ -25,57 +29,42 @@ __device__ __forceinline__ float axpy_op(float y, float x, float alpha) {
     else return x86_add(y, x86_mul(alpha, x));
 }
 
-// Lane-contiguous quads: lane l owns elements 4(q0 + l) .. +3, so every
-// warp access is one contiguous span; each thread keeps kUnroll quads of y
-// and of x in flight.
-constexpr int kUnroll = 4;
-
+// y = y + alpha * x on the streaming engine: y is source 1 (and the
+// destination, written back in place), x source 2; a lane step is 8 BF16/F16
+// or 4 float32 elements of each.
 template <int DT, int FUSED>
-__device__ __forceinline__ void axpy_quad(void* y, const uint32_t* yw, const uint32_t* xw, int64_t q, float alpha) {
-    constexpr int B = dtype_bytes(DT);
-    float vy[4], vx[4];
-    decode4<DT>(yw, vy);
-    decode4<DT>(xw, vx);
+struct AxpyOp {
+    static constexpr int kIn = dtype_bytes(DT);
+    static constexpr int kIn2 = kIn;
+    static constexpr int kLane = lane_elems<kIn, kIn>();
+    static constexpr int kQ = kLane / 4;
+    static constexpr bool kDefers = false;
+    static constexpr bool kPrologue = false;
+    struct State {
+        float alpha;
+    };
+    template <class A>
+    __device__ static State setup(const A& a, const ChunkRec&) {
+        return {a.scalar};
+    }
+    __device__ static void step2(const uint8_t* sy, const uint8_t* sx, const ChunkRec& ch, int64_t e, const State& st) {
+        float vy[2][4], vx[2][4];
+        load_decode_lane<DT, kQ>(sy, vy);
+        load_decode_lane<DT, kQ>(sx, vx);
+        uint32_t o[kQ * kIn];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) vy[k] = axpy_op<FUSED>(vy[k], vx[k], alpha);
-    uint32_t o[B];
-    encode4<DT>(vy, o, 0);
-    store4_stream<B>(static_cast<uint8_t*>(y) + q * 4 * B, o);
-}
-
-template <int DT, int FUSED>
-__global__ void __launch_bounds__(kThreads) axpy_vec_kernel(void* y, const void* __restrict__ x,
-                                                           int64_t n, float alpha) {
-    constexpr int B = dtype_bytes(DT);
-    const int64_t nq = n / 4;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    const uint8_t* yb = static_cast<const uint8_t*>(y);
-    const uint8_t* xb = static_cast<const uint8_t*>(x);
-    int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    for (; q + (kUnroll - 1) * stride < nq; q += kUnroll * stride) {
-        uint32_t yw[kUnroll][B], xw[kUnroll][B];
+        for (int k = 0; k < kQ; ++k) {
 #pragma unroll
-        for (int j = 0; j < kUnroll; ++j) {
-            load4_cs<B>(yb + (q + j * stride) * 4 * B, yw[j]);
-            load4_stream<B>(xb + (q + j * stride) * 4 * B, xw[j]);
+            for (int j = 0; j < 4; ++j) vy[k][j] = axpy_op<FUSED>(vy[k][j], vx[k][j], st.alpha);
+            encode4<DT>(vy[k], o + k * kIn, 0);
         }
-#pragma unroll
-        for (int j = 0; j < kUnroll; ++j) axpy_quad<DT, FUSED>(y, yw[j], xw[j], q + j * stride, alpha);
+        store_lane_stream<kLane * kIn>(static_cast<uint8_t*>(ch.dst) + e * kIn, o);
     }
-    for (; q < nq; q += stride) {
-        uint32_t yw[B], xw[B];
-        load4_cs<B>(yb + q * 4 * B, yw);
-        load4_stream<B>(xb + q * 4 * B, xw);
-        axpy_quad<DT, FUSED>(y, yw, xw, q, alpha);
+    __device__ static void element(const ChunkRec& ch, int64_t i, const State& st) {
+        const float r = axpy_op<FUSED>(load_as_f32<DT>(ch.dst, i), load_as_f32<DT>(ch.src2, i), st.alpha);
+        store_code<DT>(ch.dst, i, encode_f32<DT>(r, 0));
     }
-    if (blockIdx.x == 0) {
-        const int64_t i = nq * 4 + threadIdx.x;
-        if (i < n) {
-            const float r = axpy_op<FUSED>(load_as_f32<DT>(y, i), load_as_f32<DT>(x, i), alpha);
-            store_code<DT>(y, i, encode_f32<DT>(r, 0));
-        }
-    }
-}
+};
 
 template <int DT, int FUSED>
 __global__ void __launch_bounds__(kThreads) axpy_scalar_kernel(void* __restrict__ y, const void* __restrict__ x,
@@ -90,9 +79,14 @@ __global__ void __launch_bounds__(kThreads) axpy_scalar_kernel(void* __restrict_
 template <int DT>
 int launch_axpy(void* y, const void* x, int64_t n, float alpha, int fused, cudaStream_t s) {
     if (aligned16(y) && aligned16(x)) {
-        const int64_t blocks = stream_grid(n / 4 / kUnroll + 1, kThreads, 8);
-        if (fused) axpy_vec_kernel<DT, 1><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(y, x, n, alpha);
-        else axpy_vec_kernel<DT, 0><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(y, x, n, alpha);
+        StreamArgs<1> a{};
+        single_chunk(a, y, y, n, true, StreamGeometry<AxpyOp<DT, 0>>::kTileElems);
+        a.chunk[0].src2 = x;
+        a.scalar = alpha;
+        const cudaError_t e = fused ? launch_stream<AxpyOp<DT, 1>, 1>(a, state().sm_count, s)
+                                    : launch_stream<AxpyOp<DT, 0>, 1>(a, state().sm_count, s);
+        if (e != cudaSuccess) return cuda_fail(e, "mf_axpy launch");
+        return MF_OK;
     } else {
         const int64_t blocks = stream_grid(n, kThreads, 8);
         if (fused) axpy_scalar_kernel<DT, 1><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(y, x, n, alpha);
@@ -112,45 +106,40 @@ __device__ __forceinline__ float scalar_op(float v, float s) {
     else return x86_div(v, s);
 }
 
+// out = src (op) scalar on the streaming engine (one source).
 template <int SRC, int DST, int OP>
-__global__ void __launch_bounds__(kThreads) scalar_vec_kernel(const void* __restrict__ src, void* __restrict__ dst,
-                                                             int64_t n, float scalar) {
-    constexpr int BI = dtype_bytes(SRC), BO = dtype_bytes(DST);
-    const int64_t nq = n / 4;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    const uint8_t* sb = static_cast<const uint8_t*>(src);
-    int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    for (; q + (kUnroll - 1) * stride < nq; q += kUnroll * stride) {
-        uint32_t w[kUnroll][BI];
+struct ScalarOp {
+    static constexpr int kIn = dtype_bytes(SRC);
+    static constexpr int kOut = dtype_bytes(DST);
+    static constexpr int kIn2 = 0;
+    static constexpr int kLane = lane_elems<kIn, kOut>();
+    static constexpr int kQ = kLane / 4;
+    static constexpr bool kDefers = false;
+    static constexpr bool kPrologue = false;
+    struct State {
+        float s;
+    };
+    template <class A>
+    __device__ static State setup(const A& a, const ChunkRec&) {
+        return {a.scalar};
+    }
+    template <bool DEFER>
+    __device__ static void step(const uint8_t* sp, const ChunkRec& ch, int64_t e, const State& st, FixQueue&) {
+        float v[2][4];
+        load_decode_lane<SRC, kQ>(sp, v);
+        uint32_t o[kQ * kOut];
 #pragma unroll
-        for (int j = 0; j < kUnroll; ++j) load4_cs<BI>(sb + (q + j * stride) * 4 * BI, w[j]);
+        for (int k = 0; k < kQ; ++k) {
 #pragma unroll
-        for (int j = 0; j < kUnroll; ++j) {
-            float v[4];
-            decode4<SRC>(w[j], v);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) v[k] = scalar_op<OP>(v[k], scalar);
-            uint32_t o[BO];
-            encode4<DST>(v, o, 0);
-            store4_stream<BO>(static_cast<uint8_t*>(dst) + (q + j * stride) * 4 * BO, o);
+            for (int j = 0; j < 4; ++j) v[k][j] = scalar_op<OP>(v[k][j], st.s);
+            encode4<DST>(v[k], o + k * kOut, 0);
         }
+        store_lane_stream<kLane * kOut>(static_cast<uint8_t*>(ch.dst) + e * kOut, o);
     }
-    for (; q < nq; q += stride) {
-        uint32_t w[BI];
-        load4_cs<BI>(sb + q * 4 * BI, w);
-        float v[4];
-        decode4<SRC>(w, v);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = scalar_op<OP>(v[k], scalar);
-        uint32_t o[BO];
-        encode4<DST>(v, o, 0);
-        store4_stream<BO>(static_cast<uint8_t*>(dst) + q * 4 * BO, o);
+    __device__ static void element(const ChunkRec& ch, int64_t i, const State& st) {
+        store_code<DST>(ch.dst, i, encode_f32<DST>(scalar_op<OP>(load_as_f32<SRC>(ch.src, i), st.s), 0));
     }
-    if (blockIdx.x == 0) {
-        const int64_t i = nq * 4 + threadIdx.x;
-        if (i < n) store_code<DST>(dst, i, encode_f32<DST>(scalar_op<OP>(load_as_f32<SRC>(src, i), scalar), 0));
-    }
-}
+};
 
 template <int SRC, int DST, int OP>
 __global__ void __launch_bounds__(kThreads) scalar_elem_kernel(const void* __restrict__ src, void* __restrict__ dst,
@@ -161,36 +150,39 @@ __global__ void __launch_bounds__(kThreads) scalar_elem_kernel(const void* __res
 }
 
 template <int SRC, int DST, int OP>
-void launch_scalar_op(const void* src, void* dst, int64_t n, float scalar, cudaStream_t s) {
+cudaError_t launch_scalar_op(const void* src, void* dst, int64_t n, float scalar, cudaStream_t s) {
     constexpr bool kVecSrc = SRC == MF_DT_F32 || SRC == MF_DT_F16 || SRC == MF_DT_BF16 || SRC == MF_DT_F8E4M3 ||
                              SRC == MF_DT_F8E5M2;
-    if (kVecSrc && aligned16(src) && aligned16(dst)) {
-        if constexpr (kVecSrc) {
-            const int64_t blocks = stream_grid(n / 4 / kUnroll + 1, kThreads, 8);
-            scalar_vec_kernel<SRC, DST, OP><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, scalar);
+    if constexpr (kVecSrc) {
+        if (aligned16(src) && aligned16(dst)) {
+            StreamArgs<1> a{};
+            single_chunk(a, src, dst, n, true, StreamGeometry<ScalarOp<SRC, DST, OP>>::kTileElems);
+            a.scalar = scalar;
+            return launch_stream<ScalarOp<SRC, DST, OP>, 1>(a, state().sm_count, s);
         }
-    } else {
-        const int64_t blocks = stream_grid(n, kThreads, 8);
-        scalar_elem_kernel<SRC, DST, OP><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, scalar);
     }
+    const int64_t blocks = stream_grid(n, kThreads, 8);
+    scalar_elem_kernel<SRC, DST, OP><<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(src, dst, n, scalar);
+    return cudaGetLastError();
 }
 
 template <int SRC, int DST>
-void dispatch_op(int op, const void* src, void* dst, int64_t n, float scalar, cudaStream_t s) {
+cudaError_t dispatch_op(int op, const void* src, void* dst, int64_t n, float scalar, cudaStream_t s) {
     switch (op) {
-    case MF_SCALAR_ADD: launch_scalar_op<SRC, DST, MF_SCALAR_ADD>(src, dst, n, scalar, s); break;
-    case MF_SCALAR_SUB: launch_scalar_op<SRC, DST, MF_SCALAR_SUB>(src, dst, n, scalar, s); break;
-    case MF_SCALAR_MUL: launch_scalar_op<SRC, DST, MF_SCALAR_MUL>(src, dst, n, scalar, s); break;
-    default: launch_scalar_op<SRC, DST, MF_SCALAR_DIV>(src, dst, n, scalar, s); break;
+    case MF_SCALAR_ADD: return launch_scalar_op<SRC, DST, MF_SCALAR_ADD>(src, dst, n, scalar, s);
+    case MF_SCALAR_SUB: return launch_scalar_op<SRC, DST, MF_SCALAR_SUB>(src, dst, n, scalar, s);
+    case MF_SCALAR_MUL: return launch_scalar_op<SRC, DST, MF_SCALAR_MUL>(src, dst, n, scalar, s);
+    default: return launch_scalar_op<SRC, DST, MF_SCALAR_DIV>(src, dst, n, scalar, s);
     }
 }
 
 template <int SRC>
-void dispatch_scalar_dst(int dst_dt, int op, const void* src, void* dst, int64_t n, float scalar, cudaStream_t s) {
+cudaError_t dispatch_scalar_dst(int dst_dt, int op, const void* src, void* dst, int64_t n, float scalar,
+                                cudaStream_t s) {
     switch (dst_dt) {
-    case MF_DT_F32: dispatch_op<SRC, MF_DT_F32>(op, src, dst, n, scalar, s); break;
-    case MF_DT_F16: dispatch_op<SRC, MF_DT_F16>(op, src, dst, n, scalar, s); break;
-    default: dispatch_op<SRC, MF_DT_BF16>(op, src, dst, n, scalar, s); break;
+    case MF_DT_F32: return dispatch_op<SRC, MF_DT_F32>(op, src, dst, n, scalar, s);
+    case MF_DT_F16: return dispatch_op<SRC, MF_DT_F16>(op, src, dst, n, scalar, s);
+    default: return dispatch_op<SRC, MF_DT_BF16>(op, src, dst, n, scalar, s);
     }
 }
 
@@ -255,24 +247,25 @@ extern "C" int mf_scalar_broadcast(const void* src, int src_dtype, void* dst, in
     if (n == 0) return MF_OK;
     if (!src || !dst) return fail(MF_ERR_INVALID_ARGUMENT, "mf_scalar_broadcast: NULL buffer");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
     switch (src_dtype) {
-    case MF_DT_F32: dispatch_scalar_dst<MF_DT_F32>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_F16: dispatch_scalar_dst<MF_DT_F16>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_BF16: dispatch_scalar_dst<MF_DT_BF16>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_F8E4M3: dispatch_scalar_dst<MF_DT_F8E4M3>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_F8E5M2: dispatch_scalar_dst<MF_DT_F8E5M2>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_F64: dispatch_scalar_dst<MF_DT_F64>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_I64: dispatch_scalar_dst<MF_DT_I64>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_I32: dispatch_scalar_dst<MF_DT_I32>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_I16: dispatch_scalar_dst<MF_DT_I16>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_I8: dispatch_scalar_dst<MF_DT_I8>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_I4: dispatch_scalar_dst<MF_DT_I4>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_U64: dispatch_scalar_dst<MF_DT_U64>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_U32: dispatch_scalar_dst<MF_DT_U32>(dst_dtype, op, src, dst, n, scalar, s); break;
-    case MF_DT_U16: dispatch_scalar_dst<MF_DT_U16>(dst_dtype, op, src, dst, n, scalar, s); break;
-    default: dispatch_scalar_dst<MF_DT_U8>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_F32: e = dispatch_scalar_dst<MF_DT_F32>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_F16: e = dispatch_scalar_dst<MF_DT_F16>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_BF16: e = dispatch_scalar_dst<MF_DT_BF16>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_F8E4M3: e = dispatch_scalar_dst<MF_DT_F8E4M3>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_F8E5M2: e = dispatch_scalar_dst<MF_DT_F8E5M2>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_F64: e = dispatch_scalar_dst<MF_DT_F64>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_I64: e = dispatch_scalar_dst<MF_DT_I64>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_I32: e = dispatch_scalar_dst<MF_DT_I32>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_I16: e = dispatch_scalar_dst<MF_DT_I16>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_I8: e = dispatch_scalar_dst<MF_DT_I8>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_I4: e = dispatch_scalar_dst<MF_DT_I4>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_U64: e = dispatch_scalar_dst<MF_DT_U64>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_U32: e = dispatch_scalar_dst<MF_DT_U32>(dst_dtype, op, src, dst, n, scalar, s); break;
+    case MF_DT_U16: e = dispatch_scalar_dst<MF_DT_U16>(dst_dtype, op, src, dst, n, scalar, s); break;
+    default: e = dispatch_scalar_dst<MF_DT_U8>(dst_dtype, op, src, dst, n, scalar, s); break;
     }
-    MF_LAUNCH_CHECK("mf_scalar_broadcast launch");
+    if (e != cudaSuccess) return cuda_fail(e, "mf_scalar_broadcast launch");
     return MF_OK;
 }
 

@@ -53,7 +53,8 @@ struct ChunkRec {
     int64_t n;
     int64_t tile_begin;  // first tile of this chunk within the launch
     int32_t tensor;
-    int32_t aligned;     // src and dst 16-byte aligned
+    int32_t aligned;     // src, dst (and src2) 16-byte aligned
+    const void* src2;    // second source of a two-source op (same element count), else unused
 };
 
 struct AmaxXchg;
@@ -69,7 +70,7 @@ struct StreamArgs {
     float* out_amax;       // CastXOp writer launch: global amax [n_tensors] (or NULL)
     float* out_scale_inv;  // CastXOp writer launch: scale_inv [n_tensors] (or NULL)
     int32_t writer;        // CastXOp: this launch writes the outputs and clears the next run's scratch
-    int32_t pad;
+    float scalar;          // the scalar of AxpyOp (alpha) and ScalarOp
     ChunkRec chunk[MaxChunks];
 };
 
@@ -344,6 +345,7 @@ struct ConvertOp {
     static constexpr int kQ = kLane / 4;
     static constexpr bool kDefers = (DST == MF_DT_F8E4M3 || DST == MF_DT_F8E5M2) && COMPAT == 0;
     static constexpr bool kPrologue = false;
+    static constexpr int kIn2 = 0;  // one source
     struct State {};
     template <class A>
     __device__ static State setup(const A&, const ChunkRec&) { return {}; }
@@ -397,6 +399,7 @@ struct CastOp {
     static constexpr int kQ = kLane / 4;
     static constexpr bool kDefers = COMPAT == 0;
     static constexpr bool kPrologue = false;
+    static constexpr int kIn2 = 0;
     struct State {
         float scale;
     };
@@ -535,10 +538,20 @@ struct CastXOp : CastOp<SRC, FP8, COMPAT> {
 
 // ------------------------------------------------------------- the engine
 
+// A two-source op (kIn2 > 0) stages both sources' tiles side by side in one
+// stage: 8192 elements when both are at most 2 bytes wide (32 KB a stage), else
+// 4096 -- two stages in the same 64 KB budget.
+template <class Op>
+constexpr int64_t op_tile_elems() {
+    if constexpr (Op::kIn2 == 0) return stream_tile_elems<Op::kIn>();
+    else return (Op::kIn + Op::kIn2 <= 4) ? 8192 : 4096;
+}
+
 template <class Op>
 struct StreamGeometry {
-    static constexpr int64_t kTileElems = stream_tile_elems<Op::kIn>();
-    static constexpr int kTileBytes = static_cast<int>(kTileElems) * Op::kIn;
+    static constexpr int64_t kTileElems = op_tile_elems<Op>();
+    static constexpr int kSrc2Offset = static_cast<int>(kTileElems) * Op::kIn;  // the second source's tile
+    static constexpr int kTileBytes = static_cast<int>(kTileElems) * (Op::kIn + Op::kIn2);
     static constexpr int kStages = (kStreamSmemBudget / kTileBytes) < 8 ? (kStreamSmemBudget / kTileBytes) : 8;
     static constexpr int kFixOffset = kStages * kTileBytes + kStages * 16;  // 16-byte aligned
     static constexpr int kFixBytes = Op::kDefers ? kConsumerWarps * kFixSlots * (32 + 8) : 0;
@@ -627,9 +640,19 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
             const int64_t cnt = min(G::kTileElems, ch.n - e0);
             const uint32_t bytes = static_cast<uint32_t>((cnt * Op::kIn) & ~int64_t(15));
             if (ch.aligned && bytes > 0) {
-                mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_g2s(smem + s * G::kTileBytes, static_cast<const uint8_t*>(ch.src) + e0 * Op::kIn, bytes,
-                         &full[s]);
+                if constexpr (Op::kIn2 > 0) {
+                    const uint32_t bytes2 = static_cast<uint32_t>((cnt * Op::kIn2) & ~int64_t(15));
+                    mbar_arrive_expect_tx(&full[s], bytes + bytes2);
+                    bulk_g2s(smem + s * G::kTileBytes, static_cast<const uint8_t*>(ch.src) + e0 * Op::kIn, bytes,
+                             &full[s]);
+                    if (bytes2 > 0)
+                        bulk_g2s(smem + s * G::kTileBytes + G::kSrc2Offset,
+                                 static_cast<const uint8_t*>(ch.src2) + e0 * Op::kIn2, bytes2, &full[s]);
+                } else {
+                    mbar_arrive_expect_tx(&full[s], bytes);
+                    bulk_g2s(smem + s * G::kTileBytes, static_cast<const uint8_t*>(ch.src) + e0 * Op::kIn, bytes,
+                             &full[s]);
+                }
             } else {
                 mbar_arrive(&full[s]);  // consumers read this tile from global memory
             }
@@ -680,16 +703,27 @@ __global__ void __launch_bounds__(kStreamBlock, 3) stream_kernel(const __grid_co
 #pragma unroll
                 for (int j = 0; j < kStepsPerThread; ++j) {
                     const int q = threadIdx.x + j * kStreamThreads;
-                    Op::template step<Op::kDefers>(tp + q * Op::kLane * Op::kIn, ch, e0 + Op::kLane * q, st, fq);
+                    if constexpr (Op::kIn2 > 0)
+                        Op::step2(tp + q * Op::kLane * Op::kIn, tp + G::kSrc2Offset + q * Op::kLane * Op::kIn2, ch,
+                                  e0 + Op::kLane * q, st);
+                    else
+                        Op::template step<Op::kDefers>(tp + q * Op::kLane * Op::kIn, ch, e0 + Op::kLane * q, st, fq);
                 }
                 // fill the holes parked steps left in recent tiles' output
                 if constexpr (Op::kDefers)
                     if (fq.n && (fq.n >= kDrainSlots || ++fq.age >= kDrainTiles)) fix_drain<Op>(fq);
             } else {
-                const int copied = static_cast<int>(((cnt * Op::kIn) & ~int64_t(15)) / Op::kIn);
+                int copied = static_cast<int>(((cnt * Op::kIn) & ~int64_t(15)) / Op::kIn);
+                if constexpr (Op::kIn2 > 0)
+                    copied = min(copied, static_cast<int>(((cnt * Op::kIn2) & ~int64_t(15)) / Op::kIn2));
                 const int nsteps = copied / Op::kLane;
-                for (int q = threadIdx.x; q < nsteps; q += kStreamThreads)
-                    Op::template step<false>(tp + q * Op::kLane * Op::kIn, ch, e0 + Op::kLane * q, st, fq);
+                for (int q = threadIdx.x; q < nsteps; q += kStreamThreads) {
+                    if constexpr (Op::kIn2 > 0)
+                        Op::step2(tp + q * Op::kLane * Op::kIn, tp + G::kSrc2Offset + q * Op::kLane * Op::kIn2, ch,
+                                  e0 + Op::kLane * q, st);
+                    else
+                        Op::template step<false>(tp + q * Op::kLane * Op::kIn, ch, e0 + Op::kLane * q, st, fq);
+                }
                 const int rem = static_cast<int>(cnt) - nsteps * Op::kLane;
                 if (threadIdx.x < rem) Op::element(ch, e0 + nsteps * Op::kLane + threadIdx.x, st);
             }
@@ -751,6 +785,7 @@ inline void single_chunk(StreamArgs<1>& a, const void* src, void* dst, int64_t n
     a.chunk[0].tile_begin = 0;
     a.chunk[0].tensor = 0;
     a.chunk[0].aligned = aligned ? 1 : 0;
+    a.chunk[0].src2 = nullptr;
     a.n_chunks = 1;
     a.total_tiles = (n + tile_elems - 1) / tile_elems;
     a.status = sticky_status_ptr();

@@ -417,7 +417,7 @@ def _kernel_c4g(torch, stream_handle, peak, flush, reps) -> dict:
     times = time_launches(torch, f, reps, flush)
     # read x, write out: the copy-shaped 1:1 mix
     ceiling = probe_ceiling(torch, stream_handle, x.data_ptr(), 1, o.data_ptr(), 1, n * 2 // 16, flush)
-    line = kernel_line("mf_jit_vec (generated for Gelu(Add(Mul(x,g),b)), BF16)", 4 * n, times, peak, n, ceiling)
+    line = kernel_line("mf_jit_tma (generated for Gelu(Add(Mul(x,g),b)), BF16)", 4 * n, times, peak, n, ceiling)
     k.close()
     return {"c4g_fused_gelu_generic": line}
 

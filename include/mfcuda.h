@@ -263,7 +263,12 @@ typedef struct mf_fused_program {
  * matches one (e.g. Mul(Silu(Add(Mul(x,g),b)),y)), and emits CUDA source for
  * the expression and compiles it with NVRTC for sm_100a (the CUDA
  * counterpart of the Metal target's shader emission, codegen/metal.go:79-227;
- * 0.1-0.5 s, once per distinct program in a process).  Without NVRTC the
+ * 0.1-0.5 s, once per distinct program in a process).  The generated code
+ * has three kernels: a bulk-copy pipeline over whole tiles of the full-size
+ * inputs (16-byte aligned buffers, broadcast lengths that are multiples of 8,
+ * at least one tile per SM), an 8-elements-per-lane kernel for smaller aligned
+ * arrays, and an element-wise one for everything else.  MF_FUSED_JIT_DUMP=dir
+ * writes each generated source to dir (a debugging aid).  Without NVRTC the
  * runtime interpreter runs the program.  Needs no device. */
 int mf_fused_compile(const mf_fused_program* program, mf_fused_kernel* kernel);
 int mf_fused_destroy(mf_fused_kernel kernel);

@@ -26,7 +26,14 @@
 // for the copies it issued, and returns.
 #pragma once
 
+#include "mf_async.cuh"
 #include "mf_vec.cuh"
+
+// 1: an E4M3 lane step with a band, tie or NaN value is fixed inline with
+// e4m3_fix_quad instead of being parked in the warp's fix-up queue.
+#ifndef MF_FP8_INLINE_FIX
+#define MF_FP8_INLINE_FIX 0
+#endif
 
 namespace mf {
 
@@ -44,7 +51,6 @@ constexpr int64_t stream_tile_elems() {
     return InBytes >= 4 ? 8192 : 16384;
 }
 constexpr int kStreamSmemBudget = 64 * 1024;    // staging bytes per CTA (room for 3 CTAs per SM)
-constexpr uint32_t kMbarSpinLimit = 1u << 24;   // polls of try_wait before giving up
 constexpr int kDeviceTimeout = MF_DEVICE_TIMEOUT;  // sticky status code of a timed-out wait
 
 struct ChunkRec {
@@ -73,59 +79,6 @@ struct StreamArgs {
     float scalar;          // the scalar of AxpyOp (alpha) and ScalarOp
     ChunkRec chunk[MaxChunks];
 };
-
-// ------------------------------------------------------------ PTX helpers
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void fence_barrier_init() {
-    // make the initialised barriers visible to the async (bulk-copy) proxy
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kMbarSpinLimit; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
-}
-
-// 1-D bulk copy global -> this CTA's shared memory; completion is counted in
-// bytes on `bar`.  dst, src and bytes must be multiples of 16.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
 
 // ------------------------------------------- ordering across CTAs and GPUs
 
@@ -315,7 +268,10 @@ __device__ __forceinline__ void fp8_lane_store(const float (&v)[2][4], uint8_t* 
     } else {
         if (slow) {
 #pragma unroll
-            for (int k = 0; k < Q; ++k) o[k] = encode4_fp8_ref<FP8>(v[k]);
+            for (int k = 0; k < Q; ++k) {
+                if constexpr (FP8 == MF_DT_F8E4M3 && MF_FP8_INLINE_FIX) o[k] = e4m3_fix_quad(v[k], o[k]);
+                else o[k] = encode4_fp8_ref<FP8>(v[k]);
+            }
         }
         store_lane_stream<4 * Q>(d, o);
     }
@@ -343,7 +299,8 @@ struct ConvertOp {
     static constexpr int kOut = dtype_bytes(DST);
     static constexpr int kLane = lane_elems<kIn, kOut>();
     static constexpr int kQ = kLane / 4;
-    static constexpr bool kDefers = (DST == MF_DT_F8E4M3 || DST == MF_DT_F8E5M2) && COMPAT == 0;
+    static constexpr bool kDefers =
+        ((DST == MF_DT_F8E4M3 && !MF_FP8_INLINE_FIX) || DST == MF_DT_F8E5M2) && COMPAT == 0;
     static constexpr bool kPrologue = false;
     static constexpr int kIn2 = 0;  // one source
     struct State {};
@@ -397,7 +354,7 @@ struct CastOp {
     static constexpr int kIn = dtype_bytes(SRC);
     static constexpr int kLane = lane_elems<kIn, 1>();
     static constexpr int kQ = kLane / 4;
-    static constexpr bool kDefers = COMPAT == 0;
+    static constexpr bool kDefers = COMPAT == 0 && !(FP8 == MF_DT_F8E4M3 && MF_FP8_INLINE_FIX);
     static constexpr bool kPrologue = false;
     static constexpr int kIn2 = 0;
     struct State {

@@ -195,6 +195,71 @@ def test_generated_kernel_matches_interpreter(backend, ref, seed, monkeypatch):
     gen.close(), interp.close()
 
 
+# (tree seed or None for Gelu(Add(Mul(x, g), b)), input dtypes, broadcast lengths, output dtype, tiles per SM)
+PIPELINE_CASES = [
+    (None, [BF16, BF16, BF16], [0, 4096, 4096], BF16, 2),
+    (17, [BF16, F32, F16], [0, 0, 64], F16, 1),
+    (24, [BF16, BF16, F16], [0, 0, 4096], BF16, 1),
+    (8, [F32, BF16, BF16], [0, 4096, 0], F32, 1),
+    (9, [F32, BF16, F16], [0, 8, 4096], BF16, 1),
+]
+
+
+@pytest.mark.parametrize("case", range(len(PIPELINE_CASES)))
+def test_generated_pipeline_matches_interpreter(backend, ref, case, monkeypatch):
+    """The generated kernel's bulk-copy pipeline (mf_jit_tma: taken for 16-byte aligned buffers with at
+    least one whole tile per SM; the tile is the largest power of two whose stage of full-size inputs
+    fits 32 KB) against the interpreter: one or two full-size inputs of mixed dtypes, row-broadcast
+    inputs of several lengths, several tiles per CTA, a ragged tail finished element by element, and
+    the amax of the output."""
+    seed, dts, bc, out_dt, per_sm = PIPELINE_CASES[case]
+    import torch
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    n = sms * 16384 * per_sm + 12345  # at least one whole tile per SM whatever the tile (2048 .. 16384)
+    wire = {BF16: DType.BFLOAT16, F16: DType.FLOAT16, F32: DType.FLOAT32}
+    if seed is None:
+        f = fusion.gelu_affine_chain()
+    else:
+        f = fusion.FusionAST(random_tree(np.random.default_rng(seed), 4, 3), ["a", "b", "c"], "o")
+    ins = []
+    for j, dt in enumerate(dts):
+        m = bc[j] or n
+        v = synthetic.normal_f32(700 + 10 * case + j, m, 0.0, 2.0)
+        ins.append(v.view(np.uint32).copy() if dt == F32 else ref.convert(v, F32, dt))
+    kw = dict(in_dtypes=[wire[d] for d in dts], in_bcast=bc, out_dtype=wire[out_dt])
+    gen = fusion.emit_cuda(f, **kw)
+    assert gen.generated(), "NVRTC codegen unavailable"
+    monkeypatch.setenv("MF_FUSED_JIT", "0")
+    interp = fusion.emit_cuda(f, **kw)
+    assert interp.kind() == 0
+    osz = ITEMSIZE[out_dt]
+    bufs = [to_device(a) for a in ins]
+    outs = []
+    for k in (gen, interp):
+        d = empty(n * osz + 64)
+        am = empty(4, fill=0)
+        k.run([b.ptr for b in bufs], d.ptr, n, amax=am.ptr)
+        o = fetch(d, n * osz + 64)
+        assert (o[n * osz:] == 0xA5).all()
+        outs.append((o[:n * osz], fetch(am, 4, np.uint32)[0]))
+        d.free(), am.free()
+    if out_dt == F32:
+        bits_equal(outs[0][0], outs[1][0])
+        assert outs[0][1] == outs[1][1]
+    else:
+        g16, i16 = (o[0].view(np.uint16) for o in outs)
+        assert ulp_diff_16(g16, i16, 0x7F80 if out_dt == BF16 else 0x7C00).max() <= 1
+    for o, am in outs:
+        v = o.view({2: np.uint16, 4: np.uint32}[osz])
+        vals = ((v.astype(np.uint32) << 16).view(np.float32) if out_dt == BF16 else
+                v.view(np.float16).astype(np.float32) if out_dt == F16 else v.view(np.float32))
+        mags = np.abs(vals[~np.isnan(vals)])
+        assert am == np.float32(mags.max() if mags.size else 0.0).view(np.uint32)
+    for b in bufs:
+        b.free()
+    gen.close(), interp.close()
+
+
 @pytest.mark.parametrize("out_dt", [BF16, F16])
 @pytest.mark.parametrize("op", [N.SIGMOID, N.TANH, N.GELU, N.SILU, N.EXP, N.LOG, N.SQRT])
 def test_activations_16bit_output_within_1ulp(backend, ref, op, out_dt):

@@ -100,7 +100,10 @@ __device__ __forceinline__ uint32_t ld_word_once(const uint32_t* p) {
 // so one grid-stride loop over all words of the tensor needs no row
 // arithmetic; each thread keeps kFlatSteps words in flight (loads first, then
 // the math and the stores).
-constexpr int kFlatSteps = 4;
+#ifndef MF_INT4_FLAT_STEPS
+#define MF_INT4_FLAT_STEPS 4
+#endif
+constexpr int kFlatSteps = MF_INT4_FLAT_STEPS;
 
 template <int SDT, int ODT>
 __global__ void __launch_bounds__(kThreads) int4_dequant_flat_kernel(const uint32_t* __restrict__ q,

@@ -29,12 +29,6 @@
 #include "mf_async.cuh"
 #include "mf_vec.cuh"
 
-// 1: an E4M3 lane step with a band, tie or NaN value is fixed inline with
-// e4m3_fix_quad instead of being parked in the warp's fix-up queue.
-#ifndef MF_FP8_INLINE_FIX
-#define MF_FP8_INLINE_FIX 0
-#endif
-
 namespace mf {
 
 constexpr int kStreamThreads = 256;
@@ -268,10 +262,7 @@ __device__ __forceinline__ void fp8_lane_store(const float (&v)[2][4], uint8_t* 
     } else {
         if (slow) {
 #pragma unroll
-            for (int k = 0; k < Q; ++k) {
-                if constexpr (FP8 == MF_DT_F8E4M3 && MF_FP8_INLINE_FIX) o[k] = e4m3_fix_quad(v[k], o[k]);
-                else o[k] = encode4_fp8_ref<FP8>(v[k]);
-            }
+            for (int k = 0; k < Q; ++k) o[k] = encode4_fp8_ref<FP8>(v[k]);
         }
         store_lane_stream<4 * Q>(d, o);
     }
@@ -299,8 +290,7 @@ struct ConvertOp {
     static constexpr int kOut = dtype_bytes(DST);
     static constexpr int kLane = lane_elems<kIn, kOut>();
     static constexpr int kQ = kLane / 4;
-    static constexpr bool kDefers =
-        ((DST == MF_DT_F8E4M3 && !MF_FP8_INLINE_FIX) || DST == MF_DT_F8E5M2) && COMPAT == 0;
+    static constexpr bool kDefers = (DST == MF_DT_F8E4M3 || DST == MF_DT_F8E5M2) && COMPAT == 0;
     static constexpr bool kPrologue = false;
     static constexpr int kIn2 = 0;  // one source
     struct State {};
@@ -354,7 +344,7 @@ struct CastOp {
     static constexpr int kIn = dtype_bytes(SRC);
     static constexpr int kLane = lane_elems<kIn, 1>();
     static constexpr int kQ = kLane / 4;
-    static constexpr bool kDefers = COMPAT == 0 && !(FP8 == MF_DT_F8E4M3 && MF_FP8_INLINE_FIX);
+    static constexpr bool kDefers = COMPAT == 0;
     static constexpr bool kPrologue = false;
     static constexpr int kIn2 = 0;
     struct State {

@@ -207,25 +207,6 @@ __device__ __forceinline__ uint32_t encode4_fp8_fast(const float (&v)[4], uint32
     }
 }
 
-// The reference rule for four E4M3 codes with no scalar path: res is
-// encode4_fp8_fast's result for the quad.  Band lanes (hardware code 1..8, or
-// |v| exactly 2^-10, which the hardware rounds to 0 and the reference to 1)
-// take min(hw(2v), 8) with the sign; NaN lanes 0x7f; the rest keep res.
-__device__ __forceinline__ uint32_t e4m3_fix_quad(const float (&v)[4], uint32_t res) {
-    const uint32_t c = cvt4_fp8_satfinite<MF_DT_F8E4M3>(v[0], v[1], v[2], v[3]);
-    const uint32_t c7 = c & 0x7f7f7f7fu;
-    const uint32_t y = ((c7 + 0x77777777u) ^ 0x78787878u) & 0xf8f8f8f8u;
-    uint32_t band = bytes_from_bit7(~(((y & 0x7f7f7f7fu) + 0x7f7f7f7fu) | y) & 0x80808080u);
-    band |= (fabsf(v[0]) == 0.0009765625f ? 0x000000ffu : 0u) | (fabsf(v[1]) == 0.0009765625f ? 0x0000ff00u : 0u) |
-            (fabsf(v[2]) == 0.0009765625f ? 0x00ff0000u : 0u) | (fabsf(v[3]) == 0.0009765625f ? 0xff000000u : 0u);
-    const uint32_t c2 = cvt4_fp8_satfinite<MF_DT_F8E4M3>(v[0] + v[0], v[1] + v[1], v[2] + v[2], v[3] + v[3]) & 0x7f7f7f7fu;
-    const uint32_t ge8 = bytes_from_bit7((c2 + 0x78787878u) & 0x80808080u);
-    const uint32_t low = (c2 & ~ge8) | (0x08080808u & ge8) | (c & 0x80808080u);
-    const uint32_t out = (res & ~band) | (low & band);
-    const uint32_t nan = bytes_from_bit7((c7 + 0x01010101u) & 0x80808080u);
-    return (out & ~nan) | (0x7f7f7f7fu & nan);
-}
-
 template <int DT>
 __device__ __forceinline__ uint32_t encode4_fp8_ref(const float (&v)[4]) {
     if constexpr (DT == MF_DT_F8E4M3) return encode4_e4m3_ref(v[0], v[1], v[2], v[3]);

@@ -170,9 +170,13 @@ def test_scalar_broadcast(backend, ref, op, src, dst):
     raw = synthetic.uniform_bytes(op * 10 + src, (n + 1) // 2 if src == I4 else n * ITEMSIZE[src])
     ds = to_device(raw)
     d = empty(n * ITEMSIZE[dst])
-    call("mf_scalar_broadcast", ds.ptr, src, d.ptr, dst, n, -1.375, op, None)
-    got = fetch(d, n * ITEMSIZE[dst]).view({2: np.uint16, 4: np.uint32}[ITEMSIZE[dst]])
-    bits_equal(got, ref.scalar_broadcast(raw, src, dst, -1.375, op, n=n))
+    # random bytes hold NaN and infinity codes; the scalars add inf * 0, inf - inf and NaN operands
+    for sc in (-1.375, float("inf"), float("-inf"), float("nan"), 0.0):
+        if op == 3 and sc == 0.0:
+            continue
+        call("mf_scalar_broadcast", ds.ptr, src, d.ptr, dst, n, sc, op, None)
+        got = fetch(d, n * ITEMSIZE[dst]).view({2: np.uint16, 4: np.uint32}[ITEMSIZE[dst]])
+        bits_equal(got, ref.scalar_broadcast(raw, src, dst, sc, op, n=n))
     ds.free()
     d.free()
 

@@ -29,6 +29,30 @@ __device__ __forceinline__ float axpy_op(float y, float x, float alpha) {
     else return x86_add(y, x86_mul(alpha, x));
 }
 
+// Four elements: the products alpha * x as packed float32 pairs (each half
+// rounded like __fmul_rn), the sums as scalar __fadd_rn, which is never merged
+// with the product into a fused multiply-add (the reference rounds both); a NaN
+// result, whose payload follows the amd64 rule, is recomputed with the scalar
+// operations.
+template <int FUSED>
+__device__ __forceinline__ void axpy_quad_f32(float (&vy)[4], const float (&vx)[4], float alpha) {
+    if constexpr (FUSED) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) vy[j] = axpy_op<1>(vy[j], vx[j], alpha);
+    } else {
+        const float2 a2 = make_float2(alpha, alpha);
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {
+            const float2 p = __fmul2_rn(a2, make_float2(vx[j], vx[j + 1]));
+            const float s0 = __fadd_rn(vy[j], p.x), s1 = __fadd_rn(vy[j + 1], p.y);
+            const float r0 = (s0 != s0) ? axpy_op<0>(vy[j], vx[j], alpha) : s0;
+            const float r1 = (s1 != s1) ? axpy_op<0>(vy[j + 1], vx[j + 1], alpha) : s1;
+            vy[j] = r0;
+            vy[j + 1] = r1;
+        }
+    }
+}
+
 // y = y + alpha * x on the streaming engine: y is source 1 (and the
 // destination, written back in place), x source 2; a lane step is 8 BF16/F16
 // or 4 float32 elements of each.
@@ -54,8 +78,7 @@ struct AxpyOp {
         uint32_t o[kQ * kIn];
 #pragma unroll
         for (int k = 0; k < kQ; ++k) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) vy[k][j] = axpy_op<FUSED>(vy[k][j], vx[k][j], st.alpha);
+            axpy_quad_f32<FUSED>(vy[k], vx[k], st.alpha);
             encode4<DT>(vy[k], o + k * kIn, 0);
         }
         store_lane_stream<kLane * kIn>(static_cast<uint8_t*>(ch.dst) + e * kIn, o);

@@ -190,7 +190,11 @@ __device__ __forceinline__ uint4 swiglu8(const uint4& xv, const uint4& yv, const
     const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
     float2 t[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) t[k] = __fadd2_rn(__fmul2_rn(bf16x2_to_f32x2(xw[k]), gf[k]), bf[k]);
+    for (int k = 0; k < 4; ++k) {
+        // packed product, scalar sums: __fadd_rn is never contracted with the product
+        const float2 pr = __fmul2_rn(bf16x2_to_f32x2(xw[k]), gf[k]);
+        t[k] = make_float2(__fadd_rn(pr.x, bf[k].x), __fadd_rn(pr.y, bf[k].y));
+    }
     const uint32_t hi =
         max(__vimax3_u32(__float_as_uint(t[0].x), __float_as_uint(t[0].y), __float_as_uint(t[1].x)),
             __vimax3_u32(__float_as_uint(t[1].y), __float_as_uint(t[2].x),

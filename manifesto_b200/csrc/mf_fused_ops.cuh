@@ -143,14 +143,17 @@ __device__ __forceinline__ float fused_unary_try(float v, bool& bad) {
     }
 }
 
-// Pairs of elements with Blackwell's packed float32 arithmetic (each lane of
-// __fadd2_rn / __fmul2_rn rounds exactly like the scalar operation; a - b is
-// a + (-b), exact in IEEE arithmetic).  The generated code uses them for chains
-// with a 16-bit output, where NaN is compared as a class.
+// Pairs of elements.  Multiplies use Blackwell's packed float32 multiply (each
+// lane rounds like __fmul_rn); adds stay scalar __fadd_rn, which is never merged
+// into a fused multiply-add.  A packed multiply feeding a packed add was measured
+// on B200 to be contracted into one (a single rounding) in some compiled
+// contexts, even written as PTX with .rn, where the reference rounds the product
+// and the sum separately.  The generated code uses these for chains with a
+// 16-bit output, where NaN is compared as a class.
 template <int OP>
 __device__ __forceinline__ float2 fused_binary2(float2 a, float2 b) {
-    if constexpr (OP == NODE_ADD) return __fadd2_rn(a, b);
-    else if constexpr (OP == NODE_SUB) return __fadd2_rn(a, make_float2(-b.x, -b.y));
+    if constexpr (OP == NODE_ADD) return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+    else if constexpr (OP == NODE_SUB) return make_float2(__fsub_rn(a.x, b.x), __fsub_rn(a.y, b.y));
     else if constexpr (OP == NODE_MUL) return __fmul2_rn(a, b);
     else return make_float2(fused_binary<OP>(a.x, b.x), fused_binary<OP>(a.y, b.y));
 }
@@ -164,6 +167,8 @@ __device__ __forceinline__ float2 fused_unary2_try(float2 v, bool& bad) {
     if constexpr (OP == NODE_GELU) {
         constexpr float kM2Log2e = -2.0f * 1.4426950408889634f;
         const float2 c3 = make_float2(0.044715f, 0.044715f), k = make_float2(0.7978845608028654f, 0.7978845608028654f);
+        // the float32 approximation's own arithmetic (held to the 1-ulp bar of the 16-bit
+        // output, not to a reference rounding): packed throughout
         const float2 u = __fmul2_rn(k, __fadd2_rn(v, __fmul2_rn(__fmul2_rn(__fmul2_rn(c3, v), v), v)));
         const float2 a = __fmul2_rn(u, make_float2(kM2Log2e, kM2Log2e));
         bad |= !(u.x >= -9.0f && v.x <= 3.0e38f && u.y >= -9.0f && v.y <= 3.0e38f);

@@ -387,9 +387,9 @@ def _kernel_c4(torch, stream_handle, peak, flush, reps) -> dict:
     both = {"mix": "read 2 : write 1 (both passes)", "bytes": c1["bytes"] + c2["bytes"], "ms": c1["ms"] + c2["ms"],
             "gbs": round((c1["bytes"] + c2["bytes"]) / ((c1["ms"] + c2["ms"]) * 1e-3) / 1e9, 1),
             "kernel": "bw_probe_kernel<2,1> x 2"}
-    out["c4_fused_swiglu_fp8"] = kernel_line("swiglu_rows_kernel + stream_kernel<CastOp<BF16,E4M3>>", 9 * n, t_all,
-                                             peak, n, both)
-    out["c4_pass1_swiglu"] = kernel_line("swiglu_rows_kernel<amax>", 6 * n, t1, peak, n, c1)
+    out["c4_fused_swiglu_fp8"] = kernel_line("mf_jit_tma (SwiGLU, amax) + stream_kernel<CastOp<BF16,E4M3>>", 9 * n,
+                                             t_all, peak, n, both)
+    out["c4_pass1_swiglu"] = kernel_line("mf_jit_tma (generated for the SwiGLU chain) <amax>", 6 * n, t1, peak, n, c1)
     out["c4_pass2_cast"] = kernel_line("stream_kernel<CastOp<BF16,E4M3>>", 3 * n, t2, peak, n, c2)
     out["c4_fused_swiglu_fp8"]["single_pass_lower_bound_bytes"] = 5 * n
     k.close()

@@ -273,9 +273,12 @@ typedef struct mf_fused_program {
 int mf_fused_compile(const mf_fused_program* program, mf_fused_kernel* kernel);
 int mf_fused_destroy(mf_fused_kernel kernel);
 /* Which device code runs the kernel: 1 a hand-specialised body (the SwiGLU
- * chain), 2 CUDA source generated for this expression and compiled with NVRTC
- * for sm_100a at mf_fused_compile, 0 the runtime interpreter (used when NVRTC
- * is unavailable or MF_FUSED_JIT=0; mf_last_error then gives the reason). */
+ * chain; when its generated code's bulk-copy pipeline applies to a launch --
+ * aligned buffers, at least one tile per SM -- that pipeline runs instead,
+ * measured faster with the same codes), 2 CUDA source generated for this
+ * expression and compiled with NVRTC for sm_100a at mf_fused_compile, 0 the
+ * runtime interpreter (used when NVRTC is unavailable or MF_FUSED_JIT=0;
+ * mf_last_error then gives the reason). */
 int mf_fused_is_specialised(mf_fused_kernel kernel, int* specialised);
 /* out: n elements of out_dtype.  If d_amax is not NULL, the kernel also
  * folds max|out| (of the encoded values, NaN ignored) into *d_amax with an

@@ -46,5 +46,7 @@ JitKernel* jit_compile(const JitSpec& spec, std::string* why);
 void jit_release(JitKernel* k);
 // Launch the generated kernel (8 elements per lane when every buffer allows it).
 int jit_launch(JitKernel* k, const void* const* inputs, void* out, int64_t n, float* d_amax, cudaStream_t s);
+// Whether jit_launch runs the bulk-copy pipeline for these buffers and this size.
+bool jit_pipeline_applies(const JitKernel* k, const void* const* inputs, const void* out, int64_t n);
 
 }  // namespace mf

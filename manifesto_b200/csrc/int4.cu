@@ -100,6 +100,7 @@ __device__ __forceinline__ uint32_t ld_word_once(const uint32_t* p) {
 // so one grid-stride loop over all words of the tensor needs no row
 // arithmetic; each thread keeps kFlatSteps words in flight (loads first, then
 // the math and the stores).
+// Compile-time tunable: 8 words in flight measured the same as 4 on config 2.
 #ifndef MF_INT4_FLAT_STEPS
 #define MF_INT4_FLAT_STEPS 4
 #endif

@@ -300,6 +300,8 @@ __device__ __forceinline__ void tile_range(int64_t total, int64_t& t0, int64_t& 
 // tensor's maximum is reduced per warp and folded into amax[tensor] with one
 // atomicMax per warp when the CTA leaves the tensor.  Every mbarrier wait is
 // bounded; a wait that runs out records MF_DEVICE_TIMEOUT.
+// Compile-time tunables (the defaults are the measured choices): stages per CTA
+// and CTAs per SM; their product times 32 KB must fit the SM's shared memory.
 #ifndef MF_AMAX_STAGES
 #define MF_AMAX_STAGES 3
 #endif

@@ -22,8 +22,8 @@
 // (16384 elements of a 16-bit source, 8192 of a float32 one) and each CTA
 // walks a contiguous range of tiles, so a
 // CTA crosses few tensor boundaries and reduces its per-tensor maximum
-// once per crossing.  Pass 1 (stream_amax_kernel, one CTA per SM) has one
-// producer lane pull 32 KB tiles through a 6-stage shared-memory ring with
+// once per crossing.  Pass 1 (stream_amax_kernel, two CTAs per SM) has one
+// producer lane per CTA pull 32 KB tiles through a 3-stage shared-memory ring with
 // 1-D bulk copies; eight consumer warps copy a landed stage to registers,
 // release it at once and fold.  Pass 1 (amax) and pass 2 (cast) are one launch each
 // per 512 chunks; between them an NCCL max all-reduce of the amax vector
@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(kStreamBlock, 1) stream_amax_kernel(const __gr
     }
 }
 
-// Launch pass 1 over one argument block (the grid is at most one CTA per SM).
+// Launch pass 1 over one argument block (the grid is at most kAmaxCtas CTAs per SM).
 template <int SRC>
 cudaError_t launch_stream_amax(const AmaxArgs& args, int64_t tiles, cudaStream_t s) {
     static bool attr[64] = {};
